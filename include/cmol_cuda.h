@@ -1,0 +1,104 @@
+/*
+ * cmol_cuda.h — additive extensions of the libcmol API for the B200 engine.
+ *
+ * Nothing here changes cmol.h; every declaration is new.  These are the
+ * entry points a token-id workload, a multi-GPU deployment or a benchmark
+ * needs and that the text-only reference API (include/cmol.h:219-223 of
+ * nvlass/libcmol) cannot express.
+ */
+#ifndef CMOL_CUDA_H
+#define CMOL_CUDA_H
+
+#include "cmol.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- device selection ----------------------------------------------------
+ * GPUs used by the next cmol_load on any thread.  Sessions are spread over
+ * them at acquire time (weights are replicated, no inter-GPU traffic).
+ * Default: the environment variable CMOL_CUDA_DEVICES ("0,1,2"), else
+ * device 0.  Returns CMOL_ERR_ARGS for an invalid list. */
+cmol_err_t cmol_cuda_set_devices(const int *devices, int n);
+
+/* Engine knobs for the next cmol_load (0 keeps the default).
+ *   kv_page_tokens : tokens per KV page (default 16)
+ *   kv_pool_frac   : fraction of free device memory the KV pool may take
+ *                    when the full max_sessions * max_ctx does not fit
+ *                    (default 0.85)
+ *   max_batch      : most sessions in one decode step (default max_sessions)
+ *   use_graphs     : 1 = capture the decode step in a CUDA graph (default),
+ *                    0 = launch kernels directly (debugging)            */
+typedef struct {
+    int   kv_page_tokens;
+    float kv_pool_frac;
+    int   max_batch;
+    int   use_graphs;
+} cmol_cuda_options_t;
+void cmol_cuda_set_options(const cmol_cuda_options_t *opt);
+
+/* ---- token-id generation -------------------------------------------------
+ * cmol_generate with token ids in place of text: the same prefill, sampling,
+ * repeat window, stop rules and callback semantics (src/api.c:437-521 of the
+ * reference), minus the tokenizer step.  The callback receives ids. */
+typedef int (*cmol_id_cb_t)(int32_t token, int is_eos, void *userdata);
+
+cmol_err_t cmol_generate_ids(cmol_session_t          *s,
+                             const int32_t           *prompt,
+                             int                      n_prompt,
+                             const cmol_gen_params_t *params,
+                             cmol_id_cb_t             on_token,
+                             void                    *userdata);
+
+/* Many sessions at once from one thread: all items are admitted to the
+ * batchers together and the call returns when every item has finished.
+ * Generated ids go to out[0..n_out) (at most out_cap); `status` is the
+ * per-item cmol_generate_ids result.  Items must use distinct sessions. */
+typedef struct {
+    cmol_session_t          *session;
+    const int32_t           *prompt;
+    int                      n_prompt;
+    const cmol_gen_params_t *params;
+    int32_t                 *out;
+    int                      out_cap;
+    int                      n_out;      /* set by the call */
+    cmol_err_t               status;     /* set by the call */
+} cmol_batch_item_t;
+
+cmol_err_t cmol_generate_batch(cmol_batch_item_t *items, int n_items);
+
+/* ---- teacher forcing / introspection -------------------------------------
+ * Run one token at the session's next position and copy the logits
+ * [vocab] out (the analogue of cmol_model_forward, src/model.h:21-24). */
+cmol_err_t cmol_forward_logits(cmol_session_t *s, int32_t token, float *logits_out);
+
+int cmol_session_n_tokens(const cmol_session_t *s);
+int cmol_session_device(const cmol_session_t *s);
+int cmol_vocab_size(const cmol_model_t *m);
+int cmol_eos_id(const cmol_model_t *m);
+
+/* ---- measurement ---------------------------------------------------------
+ * Per-GPU counters since load or the last reset.  decode_ms is device time
+ * between CUDA events recorded on the engine stream around every decode
+ * step; weight_bytes is the GGUF bytes of all matrices one step streams. */
+typedef struct {
+    long long decode_steps;
+    long long decode_tokens;     /* sampled tokens                        */
+    long long prefill_tokens;    /* prompt tokens run through the model   */
+    double    decode_ms;
+    double    step_ms_last;
+    long long weight_bytes;
+    long long kv_bytes_read;     /* KV bytes the attention read (sum)     */
+    int       kernel_launches_per_step;
+    int       graph_steps;       /* steps run through a CUDA graph        */
+} cmol_cuda_stats_t;
+
+cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats_t *out);
+void       cmol_cuda_stats_reset(cmol_model_t *m);
+int        cmol_cuda_n_gpus(const cmol_model_t *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CMOL_CUDA_H */

@@ -1,0 +1,39 @@
+// attention.cuh — GQA decode attention over the paged KV cache.
+//
+// Replaces step 5 of cmol_attn_forward (src/attn.c:103-137 of the reference):
+// for every query head h of a session at position pos,
+//   out_h = sum_{t<=pos} softmax_t(q_h . k_t / sqrt(d_head)) v_t
+// with k/v of kv head h * n_kv / n_heads.  The context is split into chunks
+// of `split_tokens` (flash-decoding): CTA (split s, kv head, column) streams
+// its chunk of K and V pages once for all query heads of the group, keeps an
+// online softmax per head, and writes a partial (max, sum, acc[d_head]).  The
+// last CTA of a (column, kv head) to finish — found with an atomic counter —
+// merges the partials in split order (deterministic) and resets the counter.
+#pragma once
+#include "common.cuh"
+
+struct AttnArgs {
+    const float *q;          // [ncol][q_ld] query rows (RoPE applied)
+    long long    q_ld;
+    float       *out;        // [ncol][out_ld]
+    long long    out_ld;
+    const int   *pos;        // [ncol]; < 0 = inactive column
+    const int   *slot;       // [ncol] -> page-table row
+    const int   *page_table; // [slots][max_pages]
+    int          max_pages;
+    const float *kv_pages;
+    long long    page_floats;
+    int          layer, n_heads, n_kv, d_head, page_tokens;
+    int          split_tokens;   // multiple of page_tokens
+    int          n_splits;       // gridDim.x
+    float        scale;          // 1/sqrt(d_head)
+    float       *part;           // scratch [ncol][n_heads][n_splits][d_head + 2]
+    int         *counters;       // scratch [ncol][n_kv], zero between launches
+};
+
+// Scratch floats / ints attention needs for ncol columns.
+inline size_t attn_part_floats(int ncol, int n_heads, int n_splits, int d_head) {
+    return (size_t)ncol * n_heads * n_splits * (d_head + 2);
+}
+
+cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl);

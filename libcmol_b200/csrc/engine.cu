@@ -1,0 +1,539 @@
+// engine.cu — one GPU's decode engine (see engine.h).
+#include "engine.h"
+
+#include <math.h>
+#include <stdarg.h>
+#include <string.h>
+
+#include <map>
+#include <string>
+
+#include "attention.cuh"
+#include "gemv_launch.cuh"
+#include "step_kernels.cuh"
+
+namespace cmolrt {
+
+namespace {
+
+// A device weight plus the allocation backing it.
+struct DevWeight {
+    QWeight q = {};
+    void   *base = nullptr;
+};
+
+struct Layer {
+    DevWeight qkv;              // fused [D + 2*KVD] rows when q/k/v share a dtype
+    DevWeight q, k, v;          // otherwise separate
+    bool      fused_qkv = false;
+    DevWeight wo, gu, down;     // gu: interleaved gate/up rows
+    float    *attn_norm = nullptr, *ffn_norm = nullptr;
+    float    *q_norm = nullptr, *k_norm = nullptr;
+};
+
+}  // namespace
+
+struct Engine::Impl {
+    HParams             hp;
+    std::vector<Layer>  layers;
+    DevWeight           embd, head;       // head.base == nullptr when tied
+    float              *out_norm = nullptr;
+    float2             *rope_cs = nullptr;
+    float              *kv_pages = nullptr;
+    long long           page_floats = 0;
+    int                *page_table = nullptr;
+    SlotSampler        *slots = nullptr;
+    // step metadata: device block and pinned mirror (same layout)
+    int                *meta_dev = nullptr, *meta_host = nullptr;
+    size_t              meta_ints = 0;
+    StepMetaPtrs        meta = {};
+    int                *out_dev = nullptr, *out_host = nullptr;
+    // activations
+    float *x = nullptr, *qbuf = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *qkvbuf = nullptr;
+    float *part = nullptr;
+    int   *counters = nullptr;
+    unsigned int *fault = nullptr;
+    int    n_splits = 1;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t  ev0 = nullptr, ev1 = nullptr;
+    std::map<int, cudaGraphExec_t> graphs;
+    std::vector<void *> allocs;
+    int launches = 0;
+};
+
+static void set_msg(char *dst, int n, const char *fmt, ...) {
+    if (!dst || n <= 0) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(dst, (size_t)n, fmt, ap);
+    va_end(ap);
+}
+
+struct EngineBuilder {
+    Engine *e;
+    Engine::Impl *d;
+    char *msg;
+    int msg_len;
+
+    template <typename T>
+    T *dalloc(size_t count, bool zero = true) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, count * sizeof(T) + 16) != cudaSuccess) return nullptr;
+        if (zero) cudaMemset(p, 0, count * sizeof(T) + 16);
+        d->allocs.push_back(p);
+        return (T *)p;
+    }
+
+    // Upload `rows` GGUF rows of dtype dt, length k, into padded planes.
+    bool upload(DevWeight &w, const uint8_t *rows_host, int dt, int rows, int k) {
+        if (!qw_nplanes(dt) || k % dt_block_values(dt) || k % 16) {
+            set_msg(msg, msg_len, "unsupported weight dtype %d / k %d", dt, k);
+            return false;
+        }
+        QWeight q = {};
+        const size_t tot = qw_layout(q, dt, rows, k, qw_default_kc(dt, k));
+        uint8_t *base = dalloc<uint8_t>(tot);
+        if (!base) { set_msg(msg, msg_len, "out of device memory (weights)"); return false; }
+        for (int i = 0; i < q.nplanes; i++) q.p[i] = base + (uintptr_t)q.p[i];
+        void *tmp = nullptr;
+        cudaError_t err = cudaMalloc(&tmp, q.bytes);
+        if (err == cudaSuccess) err = cudaMemcpy(tmp, rows_host, q.bytes, cudaMemcpyHostToDevice);
+        if (err == cudaSuccess) err = repack_launch((const uint8_t *)tmp, q, d->stream);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(d->stream);
+        if (tmp) cudaFree(tmp);
+        if (err != cudaSuccess) { set_msg(msg, msg_len, "weight upload: %s", cudaGetErrorString(err)); return false; }
+        w.q = q;
+        w.base = base;
+        return true;
+    }
+
+    float *upload_f32(const HTensor *t, int n) {
+        if (!t || t->dtype != 0 || t->nbytes < (size_t)n * 4) return nullptr;
+        float *p = dalloc<float>((size_t)n);
+        if (!p) return nullptr;
+        if (cudaMemcpy(p, t->data, (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+        return p;
+    }
+};
+
+Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, int *err, char *msg, int msg_len) {
+    const HParams &hp = m.hp;
+    *err = -4;  // CMOL_ERR_UNSUPPORTED
+    if (cudaSetDevice(device) != cudaSuccess) { set_msg(msg, msg_len, "cannot use CUDA device %d", device); return nullptr; }
+    if (hp.n_layers <= 0 || hp.d_model <= 0 || hp.n_heads <= 0 || hp.d_ffn <= 0 || hp.vocab_size <= 0 ||
+        hp.n_kv_heads <= 0 || hp.d_model % hp.n_heads || hp.n_heads % hp.n_kv_heads) {
+        *err = -3;
+        set_msg(msg, msg_len, "bad hyperparameters");
+        return nullptr;
+    }
+    const int D = hp.d_model, F = hp.d_ffn, V = hp.vocab_size, L = hp.n_layers;
+    const int hd = hp.d_head, nkv = hp.n_kv_heads, KVD = nkv * hd;
+    if (hd % 32 || hd > 256 || D > CMOLCU_GEMV_MAX_K || F > CMOLCU_GEMV_MAX_K) {
+        set_msg(msg, msg_len, "unsupported shape (d_head %d, d_model %d, d_ffn %d)", hd, D, F);
+        return nullptr;
+    }
+    Engine *e = new Engine();
+    e->device_ = device;
+    e->opt_ = o;
+    e->vocab_ = V;
+    Impl *d = new Impl();
+    e->d = d;
+    d->hp = hp;
+    EngineBuilder b{e, d, msg, msg_len};
+    auto fail = [&](int code) -> Engine * { *err = code; delete e; return nullptr; };
+
+    if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(-1);
+    cudaEventCreate(&d->ev0);
+    cudaEventCreate(&d->ev1);
+
+    // ---- weights ----------------------------------------------------------
+    const HTensor *te = m.find("token_embd.weight");
+    if (!te || te->dims[0] != D || te->dims[1] < V) { set_msg(msg, msg_len, "token_embd.weight missing or misshaped"); return fail(-3); }
+    if (!b.upload(d->embd, te->data, te->dtype, V, D)) return fail(-4);
+    long long wbytes = 0;
+    const HTensor *th = m.find("output.weight");
+    if (th) {
+        if (th->dims[0] != D) { set_msg(msg, msg_len, "output.weight misshaped"); return fail(-3); }
+        if (!b.upload(d->head, th->data, th->dtype, V, D)) return fail(-4);
+        wbytes += (long long)d->head.q.bytes;
+    } else {
+        wbytes += (long long)d->embd.q.bytes;
+    }
+    d->out_norm = b.upload_f32(m.find("output_norm.weight"), D);
+    if (!d->out_norm) { set_msg(msg, msg_len, "output_norm.weight missing"); return fail(-3); }
+
+    d->layers.resize((size_t)L);
+    std::vector<uint8_t> buf;
+    for (int l = 0; l < L; l++) {
+        Layer &ly = d->layers[(size_t)l];
+        const HTensor *wq = m.blk(l, "attn_q.weight"), *wk = m.blk(l, "attn_k.weight"),
+                      *wv = m.blk(l, "attn_v.weight"), *wo = m.blk(l, "attn_output.weight"),
+                      *wg = m.blk(l, "ffn_gate.weight"), *wu = m.blk(l, "ffn_up.weight"),
+                      *wd = m.blk(l, "ffn_down.weight");
+        if (!wq || !wk || !wv || !wo || !wg || !wu || !wd) {
+            set_msg(msg, msg_len, "layer %d: missing tensor", l);
+            return fail(-3);
+        }
+        ly.attn_norm = b.upload_f32(m.blk(l, "attn_norm.weight"), D);
+        ly.ffn_norm = b.upload_f32(m.blk(l, "ffn_norm.weight"), D);
+        if (!ly.attn_norm || !ly.ffn_norm) { set_msg(msg, msg_len, "layer %d: missing norm", l); return fail(-3); }
+        ly.q_norm = b.upload_f32(m.blk(l, "attn_q_norm.weight"), hd);
+        ly.k_norm = b.upload_f32(m.blk(l, "attn_k_norm.weight"), hd);
+        if (wq->dtype == wk->dtype && wk->dtype == wv->dtype) {
+            size_t rq = dtype_row_bytes(wq->dtype, D);
+            buf.resize(rq * (size_t)(D + 2 * KVD));
+            memcpy(buf.data(), wq->data, rq * D);
+            memcpy(buf.data() + rq * D, wk->data, rq * KVD);
+            memcpy(buf.data() + rq * (D + KVD), wv->data, rq * KVD);
+            if (!b.upload(ly.qkv, buf.data(), wq->dtype, D + 2 * KVD, D)) return fail(-4);
+            ly.fused_qkv = true;
+            wbytes += (long long)ly.qkv.q.bytes;
+        } else {
+            if (!b.upload(ly.q, wq->data, wq->dtype, D, D) || !b.upload(ly.k, wk->data, wk->dtype, KVD, D) ||
+                !b.upload(ly.v, wv->data, wv->dtype, KVD, D))
+                return fail(-4);
+            wbytes += (long long)(ly.q.q.bytes + ly.k.q.bytes + ly.v.q.bytes);
+        }
+        if (!b.upload(ly.wo, wo->data, wo->dtype, D, D)) return fail(-4);
+        if (wg->dtype != wu->dtype) { set_msg(msg, msg_len, "layer %d: gate/up dtypes differ", l); return fail(-4); }
+        {
+            size_t rg = dtype_row_bytes(wg->dtype, D);
+            buf.resize(rg * (size_t)(2 * F));
+            for (int i = 0; i < F; i++) {   // rows 2i = gate_i, 2i+1 = up_i
+                memcpy(buf.data() + rg * (2 * (size_t)i), wg->data + rg * i, rg);
+                memcpy(buf.data() + rg * (2 * (size_t)i + 1), wu->data + rg * i, rg);
+            }
+            if (!b.upload(ly.gu, buf.data(), wg->dtype, 2 * F, D)) return fail(-4);
+        }
+        if (!b.upload(ly.down, wd->data, wd->dtype, D, F)) return fail(-4);
+        wbytes += (long long)(ly.wo.q.bytes + ly.gu.q.bytes + ly.down.q.bytes);
+    }
+    e->weight_bytes_ = wbytes;
+    std::vector<uint8_t>().swap(buf);
+
+    // ---- RoPE table: theta = pos / base^(2i/d_head), src/model.c:146-148 ----
+    {
+        const int ctx = o.max_ctx;
+        std::vector<float2> cs((size_t)ctx * (hd / 2));
+        for (int p = 0; p < ctx; p++)
+            for (int i = 0; i < hd / 2; i++) {
+                float theta = (float)p / powf(hp.rope_freq_base, (float)(2 * i) / (float)hd);
+                cs[(size_t)p * (hd / 2) + i] = make_float2(cosf(theta), sinf(theta));
+            }
+        d->rope_cs = b.dalloc<float2>(cs.size());
+        if (!d->rope_cs || cudaMemcpy(d->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(-1);
+    }
+
+    // ---- activations, metadata, sampler state ------------------------------
+    const int B = o.max_batch;
+    d->x = b.dalloc<float>((size_t)B * D);
+    d->qbuf = b.dalloc<float>((size_t)B * D);
+    d->attn = b.dalloc<float>((size_t)B * D);
+    d->h = b.dalloc<float>((size_t)B * F);
+    d->logits = b.dalloc<float>((size_t)B * V);
+    d->qkvbuf = b.dalloc<float>((size_t)B * (D + 2 * KVD));
+    d->n_splits = (o.max_ctx + o.split_tokens - 1) / o.split_tokens;
+    d->part = b.dalloc<float>(attn_part_floats(B, hp.n_heads, d->n_splits, hd));
+    d->counters = b.dalloc<int>((size_t)B * nkv);
+    d->fault = b.dalloc<unsigned int>(1);
+    d->slots = b.dalloc<SlotSampler>((size_t)o.max_slots);
+    d->meta_ints = (size_t)4 * B + 1 + 3 * (size_t)B;
+    d->meta_dev = b.dalloc<int>(d->meta_ints);
+    d->out_dev = b.dalloc<int>((size_t)B);
+    if (!d->x || !d->qbuf || !d->attn || !d->h || !d->logits || !d->qkvbuf || !d->part || !d->counters ||
+        !d->fault || !d->slots || !d->meta_dev || !d->out_dev) {
+        set_msg(msg, msg_len, "out of device memory (activations)");
+        return fail(-1);
+    }
+    if (cudaMallocHost(&d->meta_host, d->meta_ints * sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&d->out_host, (size_t)B * sizeof(int)) != cudaSuccess)
+        return fail(-1);
+    d->meta.token = d->meta_dev;
+    d->meta.pos = d->meta_dev + B;
+    d->meta.slot = d->meta_dev + 2 * B;
+    d->meta.sample = d->meta_dev + 3 * B;
+    d->meta.n_upd = d->meta_dev + 4 * B;
+    d->meta.upd = d->meta_dev + 4 * B + 1;
+
+    // ---- KV page pool ------------------------------------------------------
+    const int P = o.page_tokens;
+    e->max_pages_ = (o.max_ctx + P - 1) / P;
+    d->page_floats = (long long)L * 2 * nkv * P * hd;
+    e->kv_bytes_per_token_ = (long long)L * 2 * KVD * 4;
+    d->page_table = b.dalloc<int>((size_t)o.max_slots * e->max_pages_);
+    if (!d->page_table) return fail(-1);
+    {
+        size_t fr = 0, tot = 0;
+        cudaMemGetInfo(&fr, &tot);
+        const size_t page_bytes = (size_t)d->page_floats * 4;
+        long long want = (long long)o.max_slots * e->max_pages_;
+        long long fit = (long long)((double)fr * o.kv_pool_frac / (double)page_bytes);
+        long long n = want < fit ? want : fit;
+        if (n < e->max_pages_) { set_msg(msg, msg_len, "KV pool: not enough device memory"); return fail(-1); }
+        d->kv_pages = b.dalloc<float>((size_t)n * d->page_floats, false);
+        if (!d->kv_pages) { set_msg(msg, msg_len, "KV pool allocation failed"); return fail(-1); }
+        e->n_pages_ = (int)n;
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail(-1);
+    *err = 0;
+    return e;
+}
+
+Engine::~Engine() {
+    if (!d) return;
+    cudaSetDevice(device_);
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    for (auto &kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    for (void *p : d->allocs) cudaFree(p);
+    if (d->meta_host) cudaFreeHost(d->meta_host);
+    if (d->out_host) cudaFreeHost(d->out_host);
+    if (d->ev0) cudaEventDestroy(d->ev0);
+    if (d->ev1) cudaEventDestroy(d->ev1);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    delete d;
+}
+
+unsigned int Engine::fault_code() {
+    unsigned int v = 0;
+    cudaSetDevice(device_);
+    cudaMemcpy(&v, d->fault, sizeof v, cudaMemcpyDeviceToHost);
+    if (v) cudaMemset(d->fault, 0, sizeof v);
+    return v;
+}
+
+int Engine::set_sampler(int slot, const SamplerParams &p) {
+    if (slot < 0 || slot >= opt_.max_slots) return -1;
+    SlotSampler s = {};
+    for (int i = 0; i < 4; i++) s.rng[i] = p.rng[i];
+    for (int i = 0; i < CMOLCU_REPEAT_BUF; i++) s.ring[i] = p.ring[i];
+    s.ring_head = p.ring_head;
+    s.ring_fill = p.ring_fill;
+    s.temperature = p.temperature;
+    s.top_p = p.top_p;
+    s.repeat_penalty = p.repeat_penalty;
+    s.top_k = p.top_k;
+    s.eos = p.eos;
+    cudaSetDevice(device_);
+    // synchronous: the caller's stack copy must stay valid until the copy is done
+    if (cudaMemcpyAsync(d->slots + slot, &s, sizeof s, cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+        cudaStreamSynchronize(d->stream) != cudaSuccess) {
+        snprintf(err_, sizeof err_, "set_sampler: copy failed");
+        return -1;
+    }
+    return 0;
+}
+
+// Records the kernels of one step for `ncol` columns on the engine stream.
+static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol, int max_pages, int &launches) {
+    const HParams &hp = d->hp;
+    const int D = hp.d_model, F = hp.d_ffn, V = hp.vocab_size;
+    const int hd = hp.d_head, nkv = hp.n_kv_heads, KVD = nkv * hd;
+    const cudaStream_t st = d->stream;
+    const bool pdl = true;
+    cudaError_t e;
+    launches = 0;
+    auto gemv_ncalls = [&](int n) { return (n + 1) / 2; };
+
+    StepBeginArgs sb = {};
+    sb.meta = d->meta;
+    sb.page_table = d->page_table;
+    sb.max_pages = max_pages;
+    sb.embd = d->embd.q;
+    sb.x = d->x;
+    sb.d_model = D;
+    if ((e = step_begin_launch(sb, ncol, st, false)) != cudaSuccess) return e;
+    launches++;
+
+    GemvArgs g = {};
+    g.x_inc = 1;
+    g.y_inc = 1;
+    g.eps = hp.rms_norm_eps;
+    g.fault = d->fault;
+    for (int l = 0; l < hp.n_layers; l++) {
+        const Layer &ly = d->layers[(size_t)l];
+        const bool nope = hp.no_rope_layer_interval > 0 && (l + 1) % hp.no_rope_layer_interval == 0;
+        const bool qkn = ly.q_norm || ly.k_norm;
+        // --- Q/K/V projection (+ RoPE + KV append) --------------------------
+        EpiQKV q = {};
+        q.d_model = D; q.kv_dim = KVD; q.d_head = hd; q.n_kv = nkv; q.page_tokens = o.page_tokens;
+        q.layer = l; q.rope = nope ? 0 : 1; q.rope_cs = d->rope_cs;
+        q.pos = d->meta.pos; q.slot = d->meta.slot; q.page_table = d->page_table; q.max_pages = max_pages;
+        q.kv_pages = d->kv_pages; q.page_floats = d->page_floats;
+        auto qkv_part = [&](const DevWeight &w, int row_base) -> cudaError_t {
+            GemvArgs a = g;
+            a.w = w.q;
+            a.x = d->x; a.x_ld = D;
+            a.norm_w = ly.attn_norm;
+            if (qkn) {   // raw projections; norm + RoPE + KV append in the next kernel
+                a.y = d->qkvbuf + row_base; a.y_ld = D + 2 * KVD;
+                launches += gemv_ncalls(ncol);
+                return gemv_launch_cols(a, ncol, EPI_STORE, st, pdl);
+            }
+            a.y = d->qbuf; a.y_ld = D;
+            a.qkv = q;
+            a.qkv.row_base = row_base;
+            launches += gemv_ncalls(ncol);
+            return gemv_launch_cols(a, ncol, EPI_QKV, st, pdl);
+        };
+        if (ly.fused_qkv) {
+            if ((e = qkv_part(ly.qkv, 0)) != cudaSuccess) return e;
+        } else {
+            if ((e = qkv_part(ly.q, 0)) != cudaSuccess) return e;
+            if ((e = qkv_part(ly.k, D)) != cudaSuccess) return e;
+            if ((e = qkv_part(ly.v, D + KVD)) != cudaSuccess) return e;
+        }
+        if (qkn) {
+            QkNormArgs qa = {};
+            qa.qkv = d->qkvbuf; qa.qkv_ld = D + 2 * KVD;
+            qa.q_out = d->qbuf; qa.q_ld = D;
+            qa.q_norm = ly.q_norm; qa.k_norm = ly.k_norm; qa.eps = hp.rms_norm_eps;
+            qa.e = q;
+            if ((e = qknorm_launch(qa, ncol, hp.n_heads, st, pdl)) != cudaSuccess) return e;
+            launches++;
+        }
+        // --- attention -------------------------------------------------------
+        AttnArgs at = {};
+        at.q = d->qbuf; at.q_ld = D;
+        at.out = d->attn; at.out_ld = D;
+        at.pos = d->meta.pos; at.slot = d->meta.slot;
+        at.page_table = d->page_table; at.max_pages = max_pages;
+        at.kv_pages = d->kv_pages; at.page_floats = d->page_floats;
+        at.layer = l; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;
+        at.split_tokens = o.split_tokens; at.n_splits = d->n_splits;
+        at.scale = 1.0f / sqrtf((float)hd);
+        at.part = d->part; at.counters = d->counters;
+        if ((e = attention_launch(at, ncol, st, pdl)) != cudaSuccess) return e;
+        launches++;
+        // --- output projection + residual -----------------------------------
+        {
+            GemvArgs a = g;
+            a.w = ly.wo.q;
+            a.x = d->attn; a.x_ld = D;
+            a.y = d->x; a.y_ld = D;
+            if ((e = gemv_launch_cols(a, ncol, EPI_RESID, st, pdl)) != cudaSuccess) return e;
+            launches += gemv_ncalls(ncol);
+        }
+        // --- FFN: norm + gate/up + SwiGLU, then down + residual --------------
+        {
+            GemvArgs a = g;
+            a.w = ly.gu.q;
+            a.x = d->x; a.x_ld = D;
+            a.norm_w = ly.ffn_norm;
+            a.y = d->h; a.y_ld = F;
+            if ((e = gemv_launch_cols(a, ncol, EPI_SWIGLU, st, pdl)) != cudaSuccess) return e;
+            launches += gemv_ncalls(ncol);
+        }
+        {
+            GemvArgs a = g;
+            a.w = ly.down.q;
+            a.x = d->h; a.x_ld = F;
+            a.y = d->x; a.y_ld = D;
+            if ((e = gemv_launch_cols(a, ncol, EPI_RESID, st, pdl)) != cudaSuccess) return e;
+            launches += gemv_ncalls(ncol);
+        }
+    }
+    // --- final norm + LM head, sampler ----------------------------------------
+    {
+        GemvArgs a = g;
+        a.w = d->head.base ? d->head.q : d->embd.q;
+        a.x = d->x; a.x_ld = D;
+        a.norm_w = d->out_norm;
+        a.y = d->logits; a.y_ld = V;
+        if ((e = gemv_launch_cols(a, ncol, EPI_STORE, st, pdl)) != cudaSuccess) return e;
+        launches += gemv_ncalls(ncol);
+    }
+    SampleArgs sa = {};
+    sa.meta = d->meta;
+    sa.logits = d->logits;
+    sa.vocab = V;
+    sa.slots = d->slots;
+    sa.out_ids = d->out_dev;
+    if ((e = sample_launch(sa, ncol, st, pdl)) != cudaSuccess) return e;
+    launches++;
+    return cudaSuccess;
+}
+
+int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpdate> &upd, int32_t *out_ids,
+                 float *logits_out) {
+    const int n = (int)cols.size();
+    const int B = opt_.max_batch;
+    if (n <= 0 || n > B || (int)upd.size() > B) {
+        snprintf(err_, sizeof err_, "step: bad batch (%d columns, %d page updates)", n, (int)upd.size());
+        return -1;
+    }
+    cudaSetDevice(device_);
+    int bucket = 1;
+    while (bucket < n) bucket <<= 1;
+    if (bucket > B) bucket = B;
+    int *m = d->meta_host;
+    for (int i = 0; i < B; i++) {
+        bool live = i < n;
+        m[i] = live ? cols[i].token : 0;
+        m[B + i] = live ? cols[i].pos : -1;
+        m[2 * B + i] = live ? cols[i].slot : 0;
+        m[3 * B + i] = live ? cols[i].sample : 0;
+    }
+    m[4 * B] = (int)upd.size();
+    for (size_t u = 0; u < upd.size(); u++) {
+        m[4 * B + 1 + 3 * u] = upd[u].slot;
+        m[4 * B + 2 + 3 * u] = upd[u].index;
+        m[4 * B + 3 + 3 * u] = upd[u].page;
+    }
+    cudaError_t e = cudaMemcpyAsync(d->meta_dev, d->meta_host, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice,
+                                    d->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev0, d->stream);
+    int launches = 0;
+    if (e == cudaSuccess) {
+        auto it = d->graphs.find(bucket);
+        if (!opt_.use_graphs || it == d->graphs.end()) {
+            // eager launches: always the first step of a bucket (sets kernel
+            // attributes outside any capture), every step without graphs
+            e = record_step(d, opt_, bucket, max_pages_, launches);
+            d->launches = launches;
+            if (e == cudaSuccess && opt_.use_graphs) {
+                // capture this bucket for the next steps (capture does not run)
+                cudaGraph_t g = nullptr;
+                cudaGraphExec_t ge = nullptr;
+                int l2 = 0;
+                e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
+                if (e == cudaSuccess) {
+                    cudaError_t re = record_step(d, opt_, bucket, max_pages_, l2);
+                    e = cudaStreamEndCapture(d->stream, &g);
+                    if (re != cudaSuccess) e = re;
+                }
+                if (e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
+                if (g) cudaGraphDestroy(g);
+                if (e == cudaSuccess) d->graphs[bucket] = ge;
+            }
+        } else {
+            e = cudaGraphLaunch(it->second, d->stream);
+            if (e == cudaSuccess) stats.graph_steps++;
+        }
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev1, d->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->out_host, d->out_dev, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess && logits_out)
+        e = cudaMemcpyAsync(logits_out, d->logits, (size_t)n * vocab_ * sizeof(float), cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) {
+        snprintf(err_, sizeof err_, "step: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, d->ev0, d->ev1);
+    stats.steps++;
+    stats.tokens += n;
+    int ns = 0;
+    for (int i = 0; i < n; i++) ns += cols[i].sample ? 1 : 0;
+    stats.sampled += ns;
+    if (ns == n) { stats.decode_steps++; stats.decode_ms += ms; }
+    stats.step_ms_last = ms;
+    stats.step_ms_total += ms;
+    stats.launches_per_step = d->launches;
+    if (out_ids)
+        for (int i = 0; i < n; i++) out_ids[i] = d->out_host[i];
+    return 0;
+}
+
+}  // namespace cmolrt

@@ -1,0 +1,101 @@
+// engine.h — one GPU's decode engine (C++ interface, no CUDA types).
+//
+// Owns the uploaded model, the paged KV pool, per-slot sampler state and the
+// activation buffers, and runs one decode step for a batch of columns: each
+// column is one session contributing one token (its next prompt token, or
+// the token it sampled last).  The step is captured once per batch-size
+// bucket into a CUDA graph and replayed.  The host side that decides which
+// sessions run (the batcher) lives in api.cpp.
+#pragma once
+#include <stdint.h>
+
+#include <vector>
+
+#include "host_model.h"
+
+namespace cmolrt {
+
+struct EngineOptions {
+    int   max_batch = 4;       // columns per step
+    int   max_slots = 4;       // sessions (slots) with page tables
+    int   max_ctx = 2048;      // tokens per session
+    int   page_tokens = 16;
+    float kv_pool_frac = 0.85f;
+    bool  use_graphs = true;
+    int   split_tokens = 128;  // attention context split
+};
+
+struct SamplerParams {
+    float    temperature = 0.f, top_p = 1.f, repeat_penalty = 1.f;
+    int      top_k = 0;
+    int      eos = -1;
+    uint64_t rng[4] = {0, 0, 0, 0};
+    int      ring[128];
+    int      ring_fill = 0, ring_head = 0;
+};
+
+struct StepColumn {
+    int token;
+    int pos;        // position the token is written at
+    int slot;
+    int sample;     // 1: run the sampler on this column's logits
+};
+
+struct PageUpdate {
+    int slot, index, page;
+};
+
+struct EngineStats {
+    long long steps = 0, tokens = 0, sampled = 0;
+    double    step_ms_total = 0, step_ms_last = 0;
+    long long decode_steps = 0;      // steps in which every column sampled
+    double    decode_ms = 0;         // device time of those steps
+    int       launches_per_step = 0;
+    long long graph_steps = 0;
+};
+
+class Engine {
+  public:
+    // Returns nullptr and sets *err (cmol_err_t) on failure.
+    static Engine *create(int device, const HostModel &m, const EngineOptions &o, int *err, char *msg, int msg_len);
+    ~Engine();
+
+    int  device() const { return device_; }
+    int  n_pages() const { return n_pages_; }
+    int  page_tokens() const { return opt_.page_tokens; }
+    int  max_pages_per_slot() const { return max_pages_; }
+    int  max_batch() const { return opt_.max_batch; }
+    int  vocab() const { return vocab_; }
+    long long weight_bytes_per_step() const { return weight_bytes_; }
+    long long kv_bytes_per_token() const { return kv_bytes_per_token_; }
+
+    // Writes the sampler state of `slot` (async on the engine stream).
+    int set_sampler(int slot, const SamplerParams &p);
+
+    // Runs one step.  cols.size() <= max_batch.  Page updates are applied
+    // before the step.  out_ids[i] receives the sampled token of column i
+    // (undefined for columns with sample == 0).  When logits_out is not
+    // NULL the logits of every column are copied there ([ncol][vocab]).
+    // Returns 0, or -1 with a message in last_error().
+    int step(const std::vector<StepColumn> &cols, const std::vector<PageUpdate> &upd,
+             int32_t *out_ids, float *logits_out);
+
+    const char *last_error() const { return err_; }
+    EngineStats stats;
+    void reset_stats() { stats = EngineStats(); }
+    unsigned int fault_code();   // device fault word (0 = none); clears it
+
+    struct Impl;      // device state (engine.cu)
+
+  private:
+    Engine() = default;
+    Impl *d = nullptr;
+    int device_ = 0;
+    EngineOptions opt_;
+    int n_pages_ = 0, max_pages_ = 0, vocab_ = 0;
+    long long weight_bytes_ = 0, kv_bytes_per_token_ = 0;
+    char err_[256] = {0};
+    friend struct EngineBuilder;
+};
+
+}  // namespace cmolrt

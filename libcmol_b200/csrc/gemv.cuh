@@ -1,0 +1,490 @@
+// gemv.cuh — dequant-dot GEMV for one or two activation columns (sm_100a,
+// CUDA cores fed by a bulk-copy pipeline).  Replaces the n=1 use of
+// kn->matmul (src/quant.c:334-566 of the reference) on the decode path.
+//
+//   y(col,row) = sum_k deq(W[row,k]) * xn(col,k)        col < NCOL
+//   xn = x                       when norm_w == NULL
+//   xn = w[k] * (x[k] * inv_rms) otherwise (RMSNorm of src/model.c:90-97,
+//                                fused into the prologue)
+//
+// Data movement.  A CTA owns row tiles of TR = 8*R rows (round robin over
+// the grid).  A tile moves in K-chunks of KC values (KC = k unless a tile
+// would not fit a few pipeline stages).  One producer warp copies each
+// (tile, K-chunk) into a shared-memory stage with cp.async.bulk — lane r
+// copies row r of every plane — and the stage's "full" mbarrier completes
+// on the transaction byte count.  A CTA's whole share of a small matrix is
+// in flight as soon as the kernel starts; weights do not depend on the
+// previous kernel, so the producer never waits for it (programmatic
+// dependent launch).  Eight consumer warps stage the activations, then each
+// takes R rows of the tile: lane l owns 16-byte payload chunks l, l+32, ...
+// of the K-chunk, loads a chunk's activations from shared memory once and
+// reuses them for its R rows.  Consumers release a stage through its
+// "empty" mbarrier.  Every wait is bounded (sync.cuh).
+//
+// Integer -> float without I2F.  A quantised value q (0..255 after biasing)
+// placed in the low bits of a 32-bit word is the float q * 2^-149 (a
+// subnormal).  The activations are stored pre-scaled by 2^85, so one fused
+// multiply-add gives q * x * 2^-64 exactly (the product inside an fma is
+// exact; FFMA keeps subnormals unless compiled with -ftz, which this build
+// never is).  Per 16-value run the bias is removed with a precomputed run
+// sum of the activations, and the per-block scale is applied once per run.
+// The final row sum is scaled back by 2^64.  This costs about one PRMT and
+// one FFMA per weight instead of a conversion, an add and an FFMA.
+#pragma once
+#include "common.cuh"
+#include "qweight.cuh"
+#include "sync.cuh"
+
+enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+
+// Epilogue of the fused Q/K/V projection: global rows [0,D) are q,
+// [D,D+KVD) k, [D+KVD,D+2KVD) v (global row = row_base + local row).  RoPE
+// rotates q and k pairs with a host-built cos/sin table; k and v rows go
+// straight into the session's KV page for position pos (src/attn.c:82-101).
+struct EpiQKV {
+    int          d_model, kv_dim, d_head, n_kv, page_tokens, layer, rope, row_base;
+    const float2 *rope_cs;      // [pos][d_head/2] (cos, sin)
+    const int   *pos;           // [ncol]; < 0 = inactive column
+    const int   *slot;          // [ncol] session slot -> page-table row
+    const int   *page_table;    // [slots][max_pages]
+    int          max_pages;
+    float       *kv_pages;      // page pool
+    long long    page_floats;   // floats per page
+};
+
+// Stage geometry, computed on the host for one launch.
+struct PipeCfg {
+    int po[4];       // plane offsets inside a stage (TR rows of a full K-chunk each)
+    int sb;          // stage bytes
+    int nstage;      // pipeline depth
+    int rows_per_cta;// contiguous rows per CTA (multiple of R)
+};
+
+struct GemvArgs {
+    QWeight       w;
+    const float  *x;  long long x_ld; int x_inc;     // x(col,i) = x[col*x_ld + i*x_inc]
+    int           ncol;
+    const float  *norm_w; float eps;
+    float        *y;  long long y_ld; int y_inc;     // y(col,r) = y[col*y_ld + r*y_inc]
+    EpiQKV        qkv;
+    PipeCfg       pc;
+    unsigned int *fault;                             // device fault word (may be NULL)
+};
+
+#define GEMV_CWARPS 8                          // consumer warps
+#define GEMV_THREADS ((GEMV_CWARPS + 1) * 32)  // + one producer warp
+#define GEMV_MAX_STAGES 8
+
+static constexpr float kXScale    = 38685626227668133590597632.0f;  // 2^85
+static constexpr float kQScaleInv = 18446744073709551616.0f;        // 2^64
+
+__device__ __forceinline__ float q_as_sub(uint32_t word, int byte) {
+    return __uint_as_float(__byte_perm(word, 0u, 0x4440u | (uint32_t)byte));
+}
+
+// 16 FMAs of one run: four words of biased bytes against 16 activations.
+__device__ __forceinline__ float dot_run16(const uint32_t w[4], const float4 *xr) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float4 xv = xr[i];
+        acc = __fmaf_rn(q_as_sub(w[i], 0), xv.x, acc);
+        acc = __fmaf_rn(q_as_sub(w[i], 1), xv.y, acc);
+        acc = __fmaf_rn(q_as_sub(w[i], 2), xv.z, acc);
+        acc = __fmaf_rn(q_as_sub(w[i], 3), xv.w, acc);
+    }
+    return acc;
+}
+
+// Spread the low 4 bits of v into bit 4 of each byte (the Q5_0 fifth bit).
+__device__ __forceinline__ uint32_t spread4_bit4(uint32_t v) {
+    return (v * 0x02040810u) & 0x10101010u;
+}
+
+// VPC: values per 16-byte payload chunk; CR: 16-value activation runs per chunk.
+template <int DT> struct Fmt;
+template <> struct Fmt<DT_Q8_0> { static constexpr int VPC = 16; static constexpr int CR = 1; };
+template <> struct Fmt<DT_Q4_0> { static constexpr int VPC = 32; static constexpr int CR = 2; };
+template <> struct Fmt<DT_Q5_0> { static constexpr int VPC = 32; static constexpr int CR = 2; };
+template <> struct Fmt<DT_Q4_K> { static constexpr int VPC = 32; static constexpr int CR = 2; };
+template <> struct Fmt<DT_Q6_K> { static constexpr int VPC = 32; static constexpr int CR = 2; };
+template <> struct Fmt<DT_F16>  { static constexpr int VPC = 16; static constexpr int CR = 1; };
+template <> struct Fmt<DT_F32>  { static constexpr int VPC = 16; static constexpr int CR = 1; };
+
+// First activation index (within the row) of the two 16-value runs of chunk c.
+template <int DT>
+__device__ __forceinline__ void chunk_runs(int c, int &r0, int &r1) {
+    if constexpr (DT == DT_Q8_0 || DT == DT_F16 || DT == DT_F32) {
+        r0 = 16 * c; r1 = r0;
+    } else if constexpr (DT == DT_Q4_0 || DT == DT_Q5_0) {
+        r0 = 32 * c; r1 = r0 + 16;                       // low / high nibbles
+    } else if constexpr (DT == DT_Q4_K) {
+        int s = c >> 3, t = c & 7;                       // sub-blocks 2j, 2j+1
+        r0 = 256 * s + 64 * (t >> 1) + 16 * (t & 1); r1 = r0 + 32;
+    } else {                                             // Q6_K
+        int s = c >> 3, t = c & 7;
+        int glo = 4 * (t >> 2) + ((t & 3) >> 1);
+        r0 = 256 * s + 32 * glo + 16 * (t & 1); r1 = r0 + 64;
+    }
+}
+
+// Q4_K 6-bit scale and min of sub-block j from the 12 packed bytes
+// (src/quant.c:125-134).  sb[0..2] hold bytes 0-3, 4-7, 8-11.
+__device__ __forceinline__ void q4k_sm(const uint32_t sb[3], int j, int &sc, int &mn) {
+    auto byte = [&](int i) -> int { return (int)((sb[i >> 2] >> (8 * (i & 3))) & 0xFFu); };
+    if (j < 4) { sc = byte(j) & 63; mn = byte(j + 4) & 63; }
+    else { sc = (byte(j + 4) & 15) | ((byte(j - 4) >> 6) << 4); mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4); }
+}
+
+// Contribution of local chunk cl (global chunk c) of stage row `tr`
+// (2^-64 domain for quantised formats, the 2^85 domain for F16/F32).
+// x0/x1: the chunk's two activation runs (scaled, 4 x float4 each),
+// s0/s1: their run sums (2^-64 domain).
+template <int DT>
+__device__ __forceinline__ float chunk_math(const uint8_t *stage, const PipeCfg &pc, const int *st, int tr, int cl,
+                                            int c, const float4 *x0, const float4 *x1, float s0, float s1) {
+    const uint8_t *P0 = stage + pc.po[0] + tr * st[0];
+    const uint8_t *P1 = stage + pc.po[1] + tr * st[1];
+    if constexpr (DT == DT_Q8_0) {
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + cl * 16);
+        float d = h2f(*reinterpret_cast<const uint16_t *>(P1 + (cl >> 1) * 2));
+        uint32_t w[4] = {pl.x ^ 0x80808080u, pl.y ^ 0x80808080u, pl.z ^ 0x80808080u, pl.w ^ 0x80808080u};
+        float acc = dot_run16(w, x0);
+        return d * __fmaf_rn(-128.f, s0, acc);
+    } else if constexpr (DT == DT_Q4_0 || DT == DT_Q5_0) {
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + cl * 16);
+        float d = h2f(*reinterpret_cast<const uint16_t *>(P1 + cl * 2));
+        uint32_t lo[4] = {pl.x & 0x0F0F0F0Fu, pl.y & 0x0F0F0F0Fu, pl.z & 0x0F0F0F0Fu, pl.w & 0x0F0F0F0Fu};
+        uint32_t hi[4] = {(pl.x >> 4) & 0x0F0F0F0Fu, (pl.y >> 4) & 0x0F0F0F0Fu,
+                          (pl.z >> 4) & 0x0F0F0F0Fu, (pl.w >> 4) & 0x0F0F0F0Fu};
+        float bias = 8.f;
+        if constexpr (DT == DT_Q5_0) {
+            const uint32_t qh = *reinterpret_cast<const uint32_t *>(stage + pc.po[2] + tr * st[2] + cl * 4);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                lo[i] |= spread4_bit4((qh >> (4 * i)) & 15u);
+                hi[i] |= spread4_bit4((qh >> (16 + 4 * i)) & 15u);
+            }
+            bias = 16.f;
+        }
+        float a0 = dot_run16(lo, x0);
+        float a1 = dot_run16(hi, x1);
+        return d * (__fmaf_rn(-bias, s0, a0) + __fmaf_rn(-bias, s1, a1));
+    } else if constexpr (DT == DT_Q4_K) {
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + cl * 16);
+        const uint4 h = *reinterpret_cast<const uint4 *>(P1 + (cl >> 3) * 16);
+        float d    = h2f((uint16_t)(h.x & 0xFFFF));
+        float dmin = h2f((uint16_t)(h.x >> 16));
+        uint32_t sb[3] = {h.y, h.z, h.w};
+        int j = (c & 7) >> 1;
+        int sc0, mn0, sc1, mn1;
+        q4k_sm(sb, 2 * j, sc0, mn0);
+        q4k_sm(sb, 2 * j + 1, sc1, mn1);
+        uint32_t lo[4] = {pl.x & 0x0F0F0F0Fu, pl.y & 0x0F0F0F0Fu, pl.z & 0x0F0F0F0Fu, pl.w & 0x0F0F0F0Fu};
+        uint32_t hi[4] = {(pl.x >> 4) & 0x0F0F0F0Fu, (pl.y >> 4) & 0x0F0F0F0Fu,
+                          (pl.z >> 4) & 0x0F0F0F0Fu, (pl.w >> 4) & 0x0F0F0F0Fu};
+        float a0 = dot_run16(lo, x0);
+        float a1 = dot_run16(hi, x1);
+        float db0 = d * (float)sc0, mb0 = dmin * (float)mn0;
+        float db1 = d * (float)sc1, mb1 = dmin * (float)mn1;
+        return __fmaf_rn(db0, a0, __fmaf_rn(-mb0, s0, __fmaf_rn(db1, a1, -mb1 * s1)));
+    } else if constexpr (DT == DT_Q6_K) {
+        const int t = c & 7, sbl = cl >> 3;
+        const int glo = 4 * (t >> 2) + ((t & 3) >> 1);
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + cl * 16);
+        const uint4 qh = *reinterpret_cast<const uint4 *>(P1 + sbl * 64 + 32 * (t >> 2) + 16 * (t & 1));
+        const int8_t *scp = reinterpret_cast<const int8_t *>(stage + pc.po[2] + tr * st[2] + sbl * 16 + 2 * glo + (t & 1));
+        float d = h2f(*reinterpret_cast<const uint16_t *>(stage + pc.po[3] + tr * st[3] + sbl * 2));
+        int sh = 2 * ((t & 3) >> 1);
+        uint32_t pw[4] = {pl.x, pl.y, pl.z, pl.w};
+        uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            lo[i] = (pw[i] & 0x0F0F0F0Fu) | (((hw[i] >> sh) & 0x03030303u) << 4);
+            hi[i] = ((pw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> (sh + 4)) & 0x03030303u) << 4);
+        }
+        float a0 = dot_run16(lo, x0);
+        float a1 = dot_run16(hi, x1);
+        float d0 = d * (float)scp[0], d1 = d * (float)scp[4];
+        return __fmaf_rn(d0, __fmaf_rn(-32.f, s0, a0), d1 * __fmaf_rn(-32.f, s1, a1));
+    } else if constexpr (DT == DT_F16) {
+        const uint4 a = *reinterpret_cast<const uint4 *>(P0 + cl * 32);
+        const uint4 b = *reinterpret_cast<const uint4 *>(P0 + cl * 32 + 16);
+        uint32_t hw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const float *xf = reinterpret_cast<const float *>(x0);
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hw[i]));
+            acc = __fmaf_rn(f.x, xf[2 * i], acc);
+            acc = __fmaf_rn(f.y, xf[2 * i + 1], acc);
+        }
+        return acc;
+    } else {  // F32
+        const float4 *w4 = reinterpret_cast<const float4 *>(P0 + cl * 64);
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float4 w = w4[i];
+            acc = __fmaf_rn(w.x, x0[i].x, acc);
+            acc = __fmaf_rn(w.y, x0[i].y, acc);
+            acc = __fmaf_rn(w.z, x0[i].z, acc);
+            acc = __fmaf_rn(w.w, x0[i].w, acc);
+        }
+        return acc;
+    }
+}
+
+template <int DT> __device__ __forceinline__ float final_scale() {
+    if constexpr (DT == DT_F16 || DT == DT_F32) return 1.0f / kXScale;
+    else return kQScaleInv;
+}
+
+// Epilogue; vals[r*NC+col] hold the totals of rows row0..row0+R-1.
+template <int NC, int R, int EPI>
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const float *vals, int lane) {
+    const int rows = a.w.rows;
+    if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
+        if (lane < R * NC) {
+            int r = lane / NC, col = lane % NC;
+            int row = row0 + r;
+            if (row < rows && col < a.ncol) {
+                float *p = a.y + (long long)col * a.y_ld + (long long)row * a.y_inc;
+                float v = vals[lane];
+                if constexpr (EPI == EPI_RESID) *p = *p + v;   // x += sublayer out (src/model.c:232,259)
+                else *p = v;
+            }
+        }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        // rows 2i (gate) and 2i+1 (up) -> h[i] = silu(g)*u   (src/model.c:117-123)
+        if (lane < (R / 2) * NC) {
+            int p = lane / NC, col = lane % NC;
+            int row = row0 + 2 * p;
+            if (row + 1 < rows && col < a.ncol) {
+                float g = vals[(2 * p) * NC + col], u = vals[(2 * p + 1) * NC + col];
+                float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                a.y[(long long)col * a.y_ld + (long long)(row / 2) * a.y_inc] = h;
+            }
+        }
+    } else {  // EPI_QKV
+        if (lane < (R / 2) * NC) {
+            const EpiQKV &e = a.qkv;
+            int p = lane / NC, col = lane % NC;
+            int row = e.row_base + row0 + 2 * p;
+            int pos = (col < a.ncol) ? e.pos[col] : -1;
+            if (row0 + 2 * p + 1 < rows && pos >= 0) {
+                float v0 = vals[(2 * p) * NC + col], v1 = vals[(2 * p + 1) * NC + col];
+                int D = e.d_model, KVD = e.kv_dim, hd = e.d_head;
+                bool is_v = row >= D + KVD;
+                if (e.rope && !is_v) {
+                    // NORM-style pair rotation, src/model.c:137-166
+                    int i = (row % hd) >> 1;
+                    float2 cs = e.rope_cs[(long long)pos * (hd / 2) + i];
+                    float n0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                    float n1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                    v0 = n0; v1 = n1;
+                }
+                if (row < D) {
+                    float *q = a.y + (long long)col * a.y_ld;
+                    q[row] = v0; q[row + 1] = v1;
+                } else {
+                    int kvr = is_v ? row - D - KVD : row - D;
+                    int head = kvr / hd, dim = kvr % hd;
+                    int srow = e.slot ? e.slot[col] : col;
+                    int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
+                    int t = pos % e.page_tokens;
+                    float *base = e.kv_pages + (long long)pg * e.page_floats +
+                                  ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd + dim;
+                    base[0] = v0; base[1] = v1;
+                }
+            }
+        }
+    }
+}
+
+// Dynamic shared memory.  Activations are stored lane-interleaved so that a
+// warp reading "run p, float4 i" of 32 consecutive chunks touches 512
+// contiguous bytes (no bank conflicts):
+//   XS[col][c / 32][p][i][c % 32]  (float4)     RS[col][c / 32][p][c % 32]
+// with c the chunk index (chunks padded to a multiple of 32).  Then the
+// stages (128-byte aligned), then 2 * GEMV_MAX_STAGES mbarriers.
+__host__ __device__ inline int gemv_chunks_padded(int k, int vpc) { return (k / vpc + 31) / 32 * 32; }
+__host__ __device__ inline size_t gemv_x_bytes(int nc, int k, int vpc, int cr) {
+    const size_t cp = (size_t)gemv_chunks_padded(k, vpc);
+    return ((size_t)nc * cp * cr * (64 + 4) + 127) & ~(size_t)127;
+}
+__host__ __device__ inline size_t gemv_smem_total(int nc, int k, int vpc, int cr, const PipeCfg &pc) {
+    return gemv_x_bytes(nc, k, vpc, cr) + (size_t)pc.nstage * pc.sb + 2 * GEMV_MAX_STAGES * 8;
+}
+
+template <int DT, int NC, int R, int EPI>
+__global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
+    constexpr int VPC = Fmt<DT>::VPC;
+    constexpr int CR = Fmt<DT>::CR;
+    constexpr int TR = GEMV_CWARPS * R;
+    static_assert(TR <= 32, "one producer lane per tile row");
+    const PipeCfg &pc = a.pc;
+    const int K = a.w.k;
+    const int C = K / VPC;
+    const int CP = gemv_chunks_padded(K, VPC);
+    float4 *XS = reinterpret_cast<float4 *>(cmolcu_smem);
+    float *RS = reinterpret_cast<float *>(XS + (size_t)NC * CP * CR * 4);
+    uint8_t *stages = cmolcu_smem + gemv_x_bytes(NC, K, VPC, CR);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(stages + (size_t)pc.nstage * pc.sb);
+    uint64_t *full = bar, *empty = bar + GEMV_MAX_STAGES;
+    __shared__ float red[GEMV_CWARPS][NC];
+    __shared__ float inv_rms[NC];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid == 0) {
+        for (int s = 0; s < pc.nstage; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], GEMV_CWARPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    // this CTA's contiguous row range, walked in stages of TR rows
+    const int row_begin = min(a.w.rows, (int)blockIdx.x * pc.rows_per_cta);
+    const int row_end = min(a.w.rows, row_begin + pc.rows_per_cta);
+    const int ntile = (row_end - row_begin + TR - 1) / TR;
+    const int nseq = ntile * a.w.nkc;
+
+    if (warp == GEMV_CWARPS) {
+        // ---------------- producer warp ----------------
+        // one bulk copy per plane and stage: rows r0..r0+nrow of K-chunk j
+        // are contiguous in the K-chunk-major layout (qweight.cuh)
+        for (int seq = 0; seq < nseq; seq++) {
+            const int s = seq % pc.nstage, n = seq / pc.nstage;
+            const int r0 = row_begin + (seq / a.w.nkc) * TR;
+            const int nrow = min(TR, row_end - r0);
+            const int j = seq % a.w.nkc;
+            if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, a.fault, FAULT_GEMV_EMPTY)) return;
+            if (lane == 0) {
+                int bytes = 0;
+#pragma unroll
+                for (int p = 0; p < 4; p++)
+                    if (p < a.w.nplanes) bytes += nrow * qw_stride(a.w, p, j);
+                mbar_arrive_expect_tx(&full[s], (uint32_t)bytes);
+                uint8_t *dst = stages + (size_t)s * pc.sb;
+#pragma unroll
+                for (int p = 0; p < 4; p++)
+                    if (p < a.w.nplanes)
+                        bulk_g2s(dst + pc.po[p], qw_row(a.w, p, j, r0), (uint32_t)(nrow * qw_stride(a.w, p, j)),
+                                 &full[s]);
+            }
+            __syncwarp();
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    pdl_wait();
+    {
+        // pass 1: RMS of each column (src/model.c:90-97), when normalising
+        if (a.norm_w) {
+            float ss[NC];
+#pragma unroll
+            for (int c = 0; c < NC; c++) ss[c] = 0.f;
+            for (int i = tid; i < K; i += GEMV_CWARPS * 32) {
+#pragma unroll
+                for (int c = 0; c < NC; c++) {
+                    float v = c < a.ncol ? a.x[(long long)c * a.x_ld + (long long)i * a.x_inc] : 0.f;
+                    ss[c] = __fmaf_rn(v, v, ss[c]);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; c++) {
+                float v = warp_sum(ss[c]);
+                if (lane == 0) red[warp][c] = v;
+            }
+            named_bar_sync(1, GEMV_CWARPS * 32);
+            if (tid < NC) {
+                float t = 0.f;
+                for (int w = 0; w < GEMV_CWARPS; w++) t += red[w][tid];
+                inv_rms[tid] = 1.0f / sqrtf(t / (float)K + a.eps);
+            }
+            named_bar_sync(1, GEMV_CWARPS * 32);
+        }
+        // pass 2: one thread per (column, chunk, run): normalise, scale by
+        // 2^85, store interleaved, and store the run sum (2^-64 domain)
+        for (int j = tid; j < NC * C * CR; j += GEMV_CWARPS * 32) {
+            const int col = j / (C * CR), rem = j % (C * CR), c = rem / CR, p = rem % CR;
+            int q0, q1;
+            chunk_runs<DT>(c, q0, q1);
+            const int r = p ? q1 : q0;
+            float v[16];
+            const float *src = a.x + (long long)col * a.x_ld + (long long)r * a.x_inc;
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = col < a.ncol ? src[(long long)i * a.x_inc] : 0.f;
+            if (a.norm_w) {
+                const float ir = inv_rms[col];
+#pragma unroll
+                for (int i = 0; i < 16; i++) v[i] = __fmul_rn(a.norm_w[r + i], __fmul_rn(v[i], ir));
+            }
+            float t = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i++) { v[i] *= kXScale; t += v[i]; }
+            float4 *dst = XS + ((size_t)col * CP * CR * 4 + (size_t)(c >> 5) * CR * 32 * 4 + (size_t)p * 4 * 32) + (c & 31);
+#pragma unroll
+            for (int i = 0; i < 4; i++) dst[i * 32] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            RS[(size_t)col * CP * CR + (size_t)(c >> 5) * CR * 32 + p * 32 + (c & 31)] = t * __int_as_float(1);
+        }
+        named_bar_sync(1, GEMV_CWARPS * 32);
+    }
+
+    int seq = 0;
+    for (int ti = 0; ti < ntile; ti++) {
+        const int row0 = row_begin + ti * TR + warp * R;
+        float acc[R * NC];
+#pragma unroll
+        for (int i = 0; i < R * NC; i++) acc[i] = 0.f;
+        for (int kci = 0; kci < a.w.nkc; kci++, seq++) {
+            const int s = seq % pc.nstage, n = seq / pc.nstage;
+            if (!mbar_wait(&full[s], n & 1, a.fault, FAULT_GEMV_FULL)) return;
+            const uint8_t *stage = stages + (size_t)s * pc.sb;
+            const int CC = qw_chunk_values(a.w, kci) / VPC;
+            const int c0 = kci * (a.w.kc / VPC);
+            int st[4];
+#pragma unroll
+            for (int p = 0; p < 4; p++) st[p] = qw_stride(a.w, p, kci);
+            if (row0 < row_end) {
+                for (int cl = lane; cl < CC; cl += 32) {
+                    const int c = c0 + cl;
+#pragma unroll
+                    for (int col = 0; col < NC; col++) {
+                        const float4 *xb = XS + (size_t)col * CP * CR * 4 + (size_t)(c >> 5) * CR * 32 * 4 + (c & 31);
+                        const float *rb = RS + (size_t)col * CP * CR + (size_t)(c >> 5) * CR * 32 + (c & 31);
+                        float4 x0[4], x1[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) x0[i] = xb[i * 32];
+                        const float s0 = rb[0];
+                        float s1 = s0;
+                        if constexpr (CR == 2) {
+#pragma unroll
+                            for (int i = 0; i < 4; i++) x1[i] = xb[(4 + i) * 32];
+                            s1 = rb[32];
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 4; i++) x1[i] = x0[i];
+                        }
+#pragma unroll
+                        for (int r = 0; r < R; r++)
+                            acc[r * NC + col] += chunk_math<DT>(stage, pc, st, warp * R + r, cl, c, x0, x1, s0, s1);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (row0 < row_end) {
+            float vals[R * NC];
+#pragma unroll
+            for (int i = 0; i < R * NC; i++) vals[i] = warp_sum(acc[i]) * final_scale<DT>();
+            gemv_epilogue<NC, R, EPI>(a, row0, vals, lane);
+        }
+    }
+}
