@@ -1,0 +1,363 @@
+"""Decode-throughput benchmark of the libcmol B200 engine.
+
+Default workload: SmolLM2-360M-shape decoder, seeded
+random weights quantised to GGUF Q4_0, one session per GPU, a 128-token
+random prompt, greedy decoding.  A "step" is one decode step: one token per
+session through all 32 layers, the LM head and the sampler.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c2|c3|c5]
+
+Multi-GPU runs are launched with torch.distributed.run, one process per GPU;
+sessions are independent (weights replicated, no collective on the data
+path), so per-GPU work is fixed as N grows ("weak" scaling).
+
+value  : decode tokens/s of the whole job = N*K / max over ranks of the
+         device time of the K steps (CUDA events around every step on the
+         engine stream, summed).
+e2e    : the same tokens over the wall time of the cmol_generate_ids call
+         that ran them (host buffers; every step copies its token ids and
+         positions host->device and the sampled ids device->host).
+roofline: the dominant kernel (the dequant-dot GEMV) measured live: all
+         GEMV launches of one decode step replayed alone from a CUDA graph
+         (cmol_cuda_gemv_sweep), GGUF bytes per launch / launch time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "c2": dict(cfg=2, prompt=128, label="config2: SmolLM2-360M-shape, GGUF Q4_0, 1 session per GPU, "
+                                        "128-token random prompt, greedy decode"),
+    "c1": dict(cfg=1, prompt=32, label="config1: SmolLM2-135M-shape, GGUF Q8_0, 1 session per GPU, "
+                                       "32-token random prompt, greedy decode"),
+}
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def model_path(spec):
+    cache = os.environ.get("CMOL_BENCH_CACHE", "/tmp/cmol_bench")
+    os.makedirs(cache, exist_ok=True)
+    return os.path.join(cache, f"{spec.name}-s{spec.seed}-ctx{spec.ctx}.gguf")
+
+
+def ensure_model(spec, rank, barrier):
+    from libcmol_b200 import synth
+    path = model_path(spec)
+    if rank == 0 and not os.path.exists(path):
+        synth.write_gguf(path, spec)
+    barrier()
+    return path
+
+
+class Clocks:
+    """nvidia-smi samples of the GPU clocks during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.p = None
+        self.rows = []
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return
+        time.sleep(0.25)
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                self.rows.append(f)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def cpu_decode_rate(path, n_threads, prompt_len, steps, seed=7):
+    """The CPU checker (oracle port) decoding on n_threads host threads, one
+    session each: aggregate decode tokens/s over a bounded sample."""
+    import numpy as np
+
+    from oracle.oracle import GenParams, OracleModel
+    om = OracleModel(path, lanes=16)
+    V = om.hp["vocab_size"]
+    rng = np.random.default_rng(seed)
+    times = [0.0] * n_threads
+
+    def work(i):
+        s = om.session(prompt_len + steps + 4)
+        prompt = rng.integers(0, V, size=prompt_len).tolist()
+        for p, t in enumerate(prompt):
+            om.forward(s, int(t), p)
+        tok = prompt[-1]
+        t0 = time.perf_counter()
+        for j in range(steps):
+            lg = om.forward(s, int(tok), prompt_len + j)
+            tok = int(lg.argmax())
+        times[i] = time.perf_counter() - t0
+        om.free_session(s)
+
+    th = [threading.Thread(target=work, args=(i,)) for i in range(n_threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    return n_threads * steps / max(times)
+
+
+def reference_decode_rate(path, n_threads, prompt_len, steps, seed=7):
+    """The unmodified reference (oracle/_ref/libcmolref.so: cmol_model_forward
+    and its argmax, as its generate loop runs them, src/api.c:448-516) on
+    n_threads host threads, one session each: aggregate decode tokens/s."""
+    import numpy as np
+
+    from oracle.oracle import ReferenceModel
+    n_threads = max(1, min(n_threads, 32))          # the reference pool holds 32 sessions
+    rm = ReferenceModel(path, prompt_len + steps + 4, max_sessions=n_threads)
+    rng = np.random.default_rng(seed)
+    sess = [rm.session() for _ in range(n_threads)]
+    times = [0.0] * n_threads
+
+    def work(i):
+        s = sess[i]
+        prompt = rng.integers(0, rm.V, size=prompt_len).tolist()
+        for p, t in enumerate(prompt):
+            rm.forward(s, int(t), p)
+        tok = prompt[-1]
+        t0 = time.perf_counter()
+        for j in range(steps):
+            tok = int(rm.forward(s, int(tok), prompt_len + j).argmax())
+        times[i] = time.perf_counter() - t0
+
+    th = [threading.Thread(target=work, args=(i,)) for i in range(n_threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    rm.close()
+    return n_threads * steps / max(times), n_threads
+
+
+def cpu_baseline(args, wl):
+    """Bounded CPU sample of the workload on the host cores.  The reference
+    does not implement Q4_0 (src/quant.c:298-308: its matmul returns without
+    writing), so for config 2 it runs on a Q5_0 stand-in of the same shape
+    (22 instead of 18 bytes per 32 weights); config 1 runs as specified."""
+    from libcmol_b200 import synth
+    from oracle.oracle import Reference
+    spec = synth.baseline_spec(wl["cfg"])
+    cores = os.cpu_count() or 1
+    if Reference.available():
+        if spec.dt_attn == synth.Q4_0:
+            spec.name += "-q5_0-stand-in"
+            spec.dt_attn = spec.dt_ffn = spec.dt_embd = synth.Q5_0
+        path = ensure_model(spec, 0, lambda: None)
+        rate, used = reference_decode_rate(path, cores, args.ref_prompt, args.ref_steps)
+        sample = (f"{used} host threads x 1 session, {args.ref_prompt}-token prompt then {args.ref_steps} "
+                  f"greedy decode steps of the reference's cmol_model_forward on {spec.name}")
+        return {"value": round(rate, 3), "unit": "tokens/s", "cores": used, "kind": "reference", "sample": sample}
+    path = ensure_model(spec, 0, lambda: None)
+    rate = cpu_decode_rate(path, cores, args.ref_prompt, args.ref_steps)
+    return {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{cores} host threads x 1 session, {args.ref_prompt}-token prompt then "
+                      f"{args.ref_steps} greedy decode steps of the C restatement on {spec.name}"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU implementation of the path on
+    the host cores (see cpu_baseline)."""
+    if rank != 0:
+        return
+    wl = WORKLOADS[args.workload]
+    cb = cpu_baseline(args, wl)
+    val = cb["value"]
+    print(json.dumps({
+        "impl": "reference", "metric": "decode tokens/sec (aggregate over GPUs)", "value": val,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.ref_steps, "warmup": 0,
+        "ms_per_step": round(1000.0 * cb["cores"] / val, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl["label"]},
+        "cpu_baseline": cb,
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--ref-steps", type=int, default=24)
+    ap.add_argument("--ref-prompt", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    import numpy as np
+
+    from libcmol_b200 import synth
+    from libcmol_b200.model import GenParams, Model
+
+    wl = WORKLOADS[args.workload]
+    spec = synth.baseline_spec(wl["cfg"])
+    path = ensure_model(spec, rank, barrier)
+    ctx = wl["prompt"] + args.warmup + args.steps + 8
+    rng = np.random.default_rng(1000 + rank)
+    prompt = rng.integers(0, spec.vocab_size, size=wl["prompt"]).tolist()
+
+    with Model(path, max_ctx=ctx, max_sessions=1, devices=[local]) as m:
+        s = m.acquire()
+        # warm-up: prefill + W decode steps (graphs captured, clocks up)
+        rc, ids = s.generate_ids(prompt, GenParams.make(0.0, max_new_tokens=args.warmup))
+        assert rc == 0 and len(ids) == args.warmup, (rc, ids)
+        last = ids[-1]
+        clocks = Clocks(local)
+        clocks.start()
+        barrier()
+        m.reset_stats()
+        t0 = time.perf_counter()
+        # K timed decode steps: the first forwards the last warm-up token
+        rc, ids = s.generate_ids([last], GenParams.make(0.0, max_new_tokens=args.steps))
+        t1 = time.perf_counter()
+        barrier()
+        clocks.stop()
+        assert rc == 0 and len(ids) == args.steps, (rc, len(ids))
+        st = m.stats(0)
+        dev_ms = st.decode_ms
+        wall_ms = (t1 - t0) * 1000.0
+        launches = st.kernel_launches_per_step
+        # the dominant kernel, measured live outside the timed region
+        sweep_ms, sweep_bytes, sweep_launches = m.gemv_sweep(0, reps=20)
+        s.release()
+
+    if dist is not None:
+        import torch
+        t = torch.tensor([dev_ms, wall_ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, wall_ms = float(t[0]), float(t[1])
+
+    if rank == 0:
+        n = world
+        tokens = n * args.steps
+        value = tokens / (dev_ms / 1000.0)
+        e2e = tokens / (wall_ms / 1000.0)
+        peak, peak_kind = peaks()
+        achieved = sweep_bytes / (sweep_ms / 1000.0) / 1e9
+        traffic = None
+        prof = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(prof):
+            try:
+                traffic = json.load(open(prof)).get(spec.name)
+            except ValueError:
+                traffic = None
+        cpu = None
+        if n == 1 and not args.no_cpu_baseline:
+            try:
+                cpu = cpu_baseline(args, wl)
+            except Exception as ex:      # the checker is test infrastructure; report, do not fail
+                cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                       "sample": f"unavailable: {ex}"}
+        line = {
+            "metric": "decode tokens/sec (aggregate over GPUs)",
+            "value": round(value, 2),
+            "unit": "tokens/s",
+            "n_gpus": n,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": wl["label"], "model": spec.name, "sessions_per_gpu": 1,
+                       "prompt_tokens": wl["prompt"], "decode_tokens_timed": args.steps,
+                       "weights_bytes_per_step": sweep_bytes,
+                       "l2": "weights streamed per step exceed the 126 MB L2 (no flush needed)"
+                             if sweep_bytes > 126e6 else "weights fit in L2: steady state, not flushed"},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * (4 * 1 + 1 + 3),
+                    "d2h_bytes_per_step": 4 * 2},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "k_gemv (all GEMV launches of one decode step, graph replay)",
+                         "peak_source": peak_kind,
+                         "bytes_per_launch": int(sweep_bytes // max(1, sweep_launches)),
+                         "launch_us": round(1000.0 * sweep_ms / max(1, sweep_launches), 3)},
+            "cpu_baseline": cpu,
+            "gpu_launches": int(args.steps * launches),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -95,6 +95,14 @@ typedef struct {
 } cmol_cuda_stats_t;
 
 cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats_t *out);
+
+/* The GEMV launches of one single-session decode step (every weight matrix
+ * streamed once) replayed `reps` times alone from a CUDA graph on GPU
+ * `gpu_index`; device milliseconds per pass from CUDA events, the GGUF bytes
+ * of the matrices and the number of launches per pass.  Must not overlap a
+ * generation on that GPU (CMOL_ERR_NO_SESSION if one is running). */
+cmol_err_t cmol_cuda_gemv_sweep(cmol_model_t *m, int gpu_index, int reps, double *ms_per_pass,
+                                long long *bytes_per_pass, int *launches_per_pass);
 void       cmol_cuda_stats_reset(cmol_model_t *m);
 int        cmol_cuda_n_gpus(const cmol_model_t *m);
 

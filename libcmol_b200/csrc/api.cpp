@@ -599,6 +599,8 @@ static cmol_err_t submit_and_wait(cmol_session_t *s, Request &r, cmol_id_cb_t cb
             aborted = true;
         }
     }
+    // the worker no longer touches the session once the request finished
+    if (aborted) s->n_tokens = r.final_n_tokens;
     return r.status;
 }
 
@@ -728,3 +730,19 @@ extern "C" const char *cmolcu_tokenizer_decode(const cmolcu_tokenizer *t, int32_
 }
 
 extern "C" void cmolcu_tokenizer_free(cmolcu_tokenizer *t) { delete t; }
+
+extern "C" cmol_err_t cmol_cuda_gemv_sweep(cmol_model_t *m, int g, int reps, double *ms_per_pass,
+                                          long long *bytes_per_pass, int *launches_per_pass) {
+    if (!m || g < 0 || g >= (int)m->workers.size() || reps <= 0 || !ms_per_pass || !bytes_per_pass ||
+        !launches_per_pass)
+        return CMOL_ERR_ARGS;
+    Worker *w = m->workers[(size_t)g].get();
+    // run on the worker's engine while no request is active on it
+    std::lock_guard<std::mutex> lk(w->mu);
+    if (!w->active.empty() || !w->incoming.empty()) return CMOL_ERR_NO_SESSION;
+    if (w->eng->gemv_sweep(reps, ms_per_pass, bytes_per_pass, launches_per_pass)) {
+        logf(m, CMOL_LOG_ERROR, "%s", w->eng->last_error());
+        return CMOL_ERR_INVALID;
+    }
+    return CMOL_OK;
+}

@@ -48,7 +48,12 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attn(AttnArgs a) {
     const long long v_plane = (long long)a.n_kv * P * hd;                            // V follows K
 
     for (int t = t0 + warp; t < t1; t += ATTN_WARPS) {
-        const float *kp = a.kv_pages + (long long)pt[t / P] * a.page_floats + kv_head_off +
+        const int pg = pt[t / P];
+        if (pg < 0 || pg >= a.n_pages) {             // never read outside the pool
+            if (lane == 0 && a.fault) atomicExch(a.fault, 4u);
+            continue;
+        }
+        const float *kp = a.kv_pages + (long long)pg * a.page_floats + kv_head_off +
                           (long long)(t % P) * hd + lane * E;
         const float *vp = kp + v_plane;
         float k[E], v[E];

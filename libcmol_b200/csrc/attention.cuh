@@ -23,6 +23,8 @@ struct AttnArgs {
     int          max_pages;
     const float *kv_pages;
     long long    page_floats;
+    int          n_pages;        // pages in the pool (bounds check)
+    unsigned int *fault;         // device fault word
     int          layer, n_heads, n_kv, d_head, page_tokens;
     int          split_tokens;   // multiple of page_tokens
     int          n_splits;       // gridDim.x

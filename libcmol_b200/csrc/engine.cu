@@ -54,6 +54,7 @@ struct Engine::Impl {
     int   *counters = nullptr;
     unsigned int *fault = nullptr;
     int    n_splits = 1;
+    long long n_pages = 0;
     cudaStream_t stream = nullptr;
     cudaEvent_t  ev0 = nullptr, ev1 = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
@@ -75,12 +76,17 @@ struct EngineBuilder {
     char *msg;
     int msg_len;
 
+    // All set-up traffic goes through the engine stream: the engine's kernels
+    // run on a non-blocking stream, which does not order itself after work on
+    // the legacy default stream.
     template <typename T>
     T *dalloc(size_t count, bool zero = true) {
         void *p = nullptr;
         if (cudaMalloc(&p, count * sizeof(T) + 16) != cudaSuccess) return nullptr;
-        if (zero) cudaMemset(p, 0, count * sizeof(T) + 16);
         d->allocs.push_back(p);
+        if (zero && (cudaMemsetAsync(p, 0, count * sizeof(T) + 16, d->stream) != cudaSuccess ||
+                     cudaStreamSynchronize(d->stream) != cudaSuccess))
+            return nullptr;
         return (T *)p;
     }
 
@@ -97,7 +103,7 @@ struct EngineBuilder {
         for (int i = 0; i < q.nplanes; i++) q.p[i] = base + (uintptr_t)q.p[i];
         void *tmp = nullptr;
         cudaError_t err = cudaMalloc(&tmp, q.bytes);
-        if (err == cudaSuccess) err = cudaMemcpy(tmp, rows_host, q.bytes, cudaMemcpyHostToDevice);
+        if (err == cudaSuccess) err = cudaMemcpyAsync(tmp, rows_host, q.bytes, cudaMemcpyHostToDevice, d->stream);
         if (err == cudaSuccess) err = repack_launch((const uint8_t *)tmp, q, d->stream);
         if (err == cudaSuccess) err = cudaStreamSynchronize(d->stream);
         if (tmp) cudaFree(tmp);
@@ -111,7 +117,9 @@ struct EngineBuilder {
         if (!t || t->dtype != 0 || t->nbytes < (size_t)n * 4) return nullptr;
         float *p = dalloc<float>((size_t)n);
         if (!p) return nullptr;
-        if (cudaMemcpy(p, t->data, (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+        if (cudaMemcpyAsync(p, t->data, (size_t)n * 4, cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+            cudaStreamSynchronize(d->stream) != cudaSuccess)
+            return nullptr;
         return p;
     }
 };
@@ -221,7 +229,9 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
                 cs[(size_t)p * (hd / 2) + i] = make_float2(cosf(theta), sinf(theta));
             }
         d->rope_cs = b.dalloc<float2>(cs.size());
-        if (!d->rope_cs || cudaMemcpy(d->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+        if (!d->rope_cs ||
+            cudaMemcpyAsync(d->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+            cudaStreamSynchronize(d->stream) != cudaSuccess)
             return fail(-1);
     }
 
@@ -236,18 +246,19 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     d->n_splits = (o.max_ctx + o.split_tokens - 1) / o.split_tokens;
     d->part = b.dalloc<float>(attn_part_floats(B, hp.n_heads, d->n_splits, hd));
     d->counters = b.dalloc<int>((size_t)B * nkv);
-    d->fault = b.dalloc<unsigned int>(1);
+
     d->slots = b.dalloc<SlotSampler>((size_t)o.max_slots);
     d->meta_ints = (size_t)4 * B + 1 + 3 * (size_t)B;
     d->meta_dev = b.dalloc<int>(d->meta_ints);
-    d->out_dev = b.dalloc<int>((size_t)B);
+    d->out_dev = b.dalloc<int>((size_t)B + 1);   // + the fault word, read back with the ids
+    d->fault = reinterpret_cast<unsigned int *>(d->out_dev + B);
     if (!d->x || !d->qbuf || !d->attn || !d->h || !d->logits || !d->qkvbuf || !d->part || !d->counters ||
         !d->fault || !d->slots || !d->meta_dev || !d->out_dev) {
         set_msg(msg, msg_len, "out of device memory (activations)");
         return fail(-1);
     }
     if (cudaMallocHost(&d->meta_host, d->meta_ints * sizeof(int)) != cudaSuccess ||
-        cudaMallocHost(&d->out_host, (size_t)B * sizeof(int)) != cudaSuccess)
+        cudaMallocHost(&d->out_host, ((size_t)B + 1) * sizeof(int)) != cudaSuccess)
         return fail(-1);
     d->meta.token = d->meta_dev;
     d->meta.pos = d->meta_dev + B;
@@ -274,6 +285,7 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
         d->kv_pages = b.dalloc<float>((size_t)n * d->page_floats, false);
         if (!d->kv_pages) { set_msg(msg, msg_len, "KV pool allocation failed"); return fail(-1); }
         e->n_pages_ = (int)n;
+        d->n_pages = n;
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(-1);
     *err = 0;
@@ -297,10 +309,14 @@ Engine::~Engine() {
 unsigned int Engine::fault_code() {
     unsigned int v = 0;
     cudaSetDevice(device_);
-    cudaMemcpy(&v, d->fault, sizeof v, cudaMemcpyDeviceToHost);
-    if (v) cudaMemset(d->fault, 0, sizeof v);
+    cudaMemcpyAsync(&v, d->fault, sizeof v, cudaMemcpyDeviceToHost, d->stream);
+    if (cudaStreamSynchronize(d->stream) == cudaSuccess && v) {
+        cudaMemsetAsync(d->fault, 0, sizeof v, d->stream);
+        cudaStreamSynchronize(d->stream);
+    }
     return v;
 }
+
 
 int Engine::set_sampler(int slot, const SamplerParams &p) {
     if (slot < 0 || slot >= opt_.max_slots) return -1;
@@ -325,7 +341,8 @@ int Engine::set_sampler(int slot, const SamplerParams &p) {
 }
 
 // Records the kernels of one step for `ncol` columns on the engine stream.
-static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol, int max_pages, int &launches) {
+static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol, int max_pages, int &launches,
+                               bool gemv_only = false) {
     const HParams &hp = d->hp;
     const int D = hp.d_model, F = hp.d_ffn, V = hp.vocab_size;
     const int hd = hp.d_head, nkv = hp.n_kv_heads, KVD = nkv * hd;
@@ -339,11 +356,16 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
     sb.meta = d->meta;
     sb.page_table = d->page_table;
     sb.max_pages = max_pages;
+    sb.max_slots = o.max_slots;
+    sb.n_pages = (int)d->n_pages;
     sb.embd = d->embd.q;
     sb.x = d->x;
     sb.d_model = D;
-    if ((e = step_begin_launch(sb, ncol, st, false)) != cudaSuccess) return e;
-    launches++;
+    sb.fault = d->fault;
+    if (!gemv_only) {
+        if ((e = step_begin_launch(sb, ncol, st, false)) != cudaSuccess) return e;
+        launches++;
+    }
 
     GemvArgs g = {};
     g.x_inc = 1;
@@ -359,7 +381,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         q.d_model = D; q.kv_dim = KVD; q.d_head = hd; q.n_kv = nkv; q.page_tokens = o.page_tokens;
         q.layer = l; q.rope = nope ? 0 : 1; q.rope_cs = d->rope_cs;
         q.pos = d->meta.pos; q.slot = d->meta.slot; q.page_table = d->page_table; q.max_pages = max_pages;
-        q.kv_pages = d->kv_pages; q.page_floats = d->page_floats;
+        q.kv_pages = d->kv_pages; q.page_floats = d->page_floats; q.n_pages = (int)d->n_pages;
         auto qkv_part = [&](const DevWeight &w, int row_base) -> cudaError_t {
             GemvArgs a = g;
             a.w = w.q;
@@ -383,7 +405,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             if ((e = qkv_part(ly.k, D)) != cudaSuccess) return e;
             if ((e = qkv_part(ly.v, D + KVD)) != cudaSuccess) return e;
         }
-        if (qkn) {
+        if (qkn && !gemv_only) {
             QkNormArgs qa = {};
             qa.qkv = d->qkvbuf; qa.qkv_ld = D + 2 * KVD;
             qa.q_out = d->qbuf; qa.q_ld = D;
@@ -398,13 +420,16 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         at.out = d->attn; at.out_ld = D;
         at.pos = d->meta.pos; at.slot = d->meta.slot;
         at.page_table = d->page_table; at.max_pages = max_pages;
-        at.kv_pages = d->kv_pages; at.page_floats = d->page_floats;
+        at.kv_pages = d->kv_pages; at.page_floats = d->page_floats; at.n_pages = (int)d->n_pages;
+        at.fault = d->fault;
         at.layer = l; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;
         at.split_tokens = o.split_tokens; at.n_splits = d->n_splits;
         at.scale = 1.0f / sqrtf((float)hd);
         at.part = d->part; at.counters = d->counters;
-        if ((e = attention_launch(at, ncol, st, pdl)) != cudaSuccess) return e;
-        launches++;
+        if (!gemv_only) {
+            if ((e = attention_launch(at, ncol, st, pdl)) != cudaSuccess) return e;
+            launches++;
+        }
         // --- output projection + residual -----------------------------------
         {
             GemvArgs a = g;
@@ -443,12 +468,14 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         if ((e = gemv_launch_cols(a, ncol, EPI_STORE, st, pdl)) != cudaSuccess) return e;
         launches += gemv_ncalls(ncol);
     }
+    if (gemv_only) return cudaSuccess;
     SampleArgs sa = {};
     sa.meta = d->meta;
     sa.logits = d->logits;
     sa.vocab = V;
     sa.slots = d->slots;
     sa.out_ids = d->out_dev;
+    sa.fault = d->fault;
     if ((e = sample_launch(sa, ncol, st, pdl)) != cudaSuccess) return e;
     launches++;
     return cudaSuccess;
@@ -512,12 +539,19 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         }
     }
     if (e == cudaSuccess) e = cudaEventRecord(d->ev1, d->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d->out_host, d->out_dev, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->out_host, d->out_dev, ((size_t)B + 1) * sizeof(int), cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess && logits_out)
         e = cudaMemcpyAsync(logits_out, d->logits, (size_t)n * vocab_ * sizeof(float), cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
     if (e != cudaSuccess) {
         snprintf(err_, sizeof err_, "step: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    const unsigned int fault = (unsigned int)d->out_host[B];
+    if (fault) {
+        cudaMemsetAsync(d->fault, 0, sizeof(unsigned int), d->stream);
+        cudaStreamSynchronize(d->stream);
+        snprintf(err_, sizeof err_, "step: device fault code %u", fault);
         return -1;
     }
     float ms = 0.f;
@@ -533,6 +567,52 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
     stats.launches_per_step = d->launches;
     if (out_ids)
         for (int i = 0; i < n; i++) out_ids[i] = d->out_host[i];
+    return 0;
+}
+
+}  // namespace cmolrt
+
+namespace cmolrt {
+
+// The GEMV launches of one single-column decode step, alone, replayed from a
+// CUDA graph: every weight matrix of the model is streamed once per pass.
+// The column is inactive (position -1), so no KV cache is written.
+int Engine::gemv_sweep(int reps, double *ms_per_pass, long long *bytes_per_pass, int *launches_per_pass) {
+    cudaSetDevice(device_);
+    const int B = opt_.max_batch;
+    int *m = d->meta_host;
+    for (int i = 0; i < B; i++) { m[i] = 0; m[B + i] = -1; m[2 * B + i] = 0; m[3 * B + i] = 0; }
+    m[4 * B] = 0;
+    int launches = 0;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t e = cudaMemcpyAsync(d->meta_dev, d->meta_host, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice,
+                                    d->stream);
+    if (e == cudaSuccess) e = record_step(d, opt_, 1, max_pages_, launches, true);   // eager warm-up
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        cudaError_t re = record_step(d, opt_, 1, max_pages_, launches, true);
+        e = cudaStreamEndCapture(d->stream, &g);
+        if (re != cudaSuccess) e = re;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
+    if (e == cudaSuccess) e = cudaGraphLaunch(ge, d->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev0, d->stream);
+    for (int r = 0; e == cudaSuccess && r < reps; r++) e = cudaGraphLaunch(ge, d->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev1, d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, d->ev0, d->ev1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        snprintf(err_, sizeof err_, "gemv_sweep: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    *ms_per_pass = (double)ms / reps;
+    *bytes_per_pass = weight_bytes_;
+    *launches_per_pass = launches;
     return 0;
 }
 

@@ -80,6 +80,10 @@ class Engine {
     int step(const std::vector<StepColumn> &cols, const std::vector<PageUpdate> &upd,
              int32_t *out_ids, float *logits_out);
 
+    // Device time of the GEMV launches of one decode step replayed alone
+    // (graph, CUDA events); bytes = GGUF bytes of all matrices streamed.
+    int gemv_sweep(int reps, double *ms_per_pass, long long *bytes_per_pass, int *launches_per_pass);
+
     const char *last_error() const { return err_; }
     EngineStats stats;
     void reset_stats() { stats = EngineStats(); }

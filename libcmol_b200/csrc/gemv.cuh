@@ -50,6 +50,7 @@ struct EpiQKV {
     int          max_pages;
     float       *kv_pages;      // page pool
     long long    page_floats;   // floats per page
+    int          n_pages;       // pages in the pool (bounds check)
 };
 
 // Stage geometry, computed on the host for one launch.
@@ -293,6 +294,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const
                     int head = kvr / hd, dim = kvr % hd;
                     int srow = e.slot ? e.slot[col] : col;
                     int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
+                    if (pg < 0 || pg >= e.n_pages) {   // never write outside the pool
+                        if (a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
+                        return;
+                    }
                     int t = pos % e.page_tokens;
                     float *base = e.kv_pages + (long long)pg * e.page_floats +
                                   ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd + dim;

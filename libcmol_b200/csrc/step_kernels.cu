@@ -64,12 +64,21 @@ __global__ void k_step_begin(StepBeginArgs a) {
         const int n = *a.meta.n_upd;
         for (int u = threadIdx.x; u < n; u += blockDim.x) {
             int s = a.meta.upd[3 * u], idx = a.meta.upd[3 * u + 1], pg = a.meta.upd[3 * u + 2];
+            if (s < 0 || s >= a.max_slots || idx < 0 || idx >= a.max_pages || pg < 0 || pg >= a.n_pages) {
+                if (a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
+                continue;
+            }
             a.page_table[(long long)s * a.max_pages + idx] = pg;
         }
     }
     if (a.meta.pos[col] < 0) return;
     const int tok = a.meta.token[col];
     float *x = a.x + (long long)col * a.d_model;
+    if (tok < 0 || tok >= a.embd.rows) {        // never read outside the table
+        if (threadIdx.x == 0 && a.fault) atomicExch(a.fault, FAULT_BAD_TOKEN);
+        for (int i = threadIdx.x; i < a.d_model; i += blockDim.x) x[i] = 0.f;
+        return;
+    }
     for (int i = threadIdx.x; i < a.d_model; i += blockDim.x) x[i] = deq_elem(a.embd, tok, i);
 }
 
@@ -121,6 +130,7 @@ __global__ void k_qknorm(QkNormArgs a, int n_heads) {
     }
     const int srow = e.slot ? e.slot[col] : col;
     const int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
+    if (pg < 0 || pg >= e.n_pages) return;
     const int t = pos % e.page_tokens;
     float *kp = e.kv_pages + (long long)pg * e.page_floats +
                 ((((long long)e.layer * 2) * e.n_kv + kh) * e.page_tokens + t) * hd;
@@ -331,6 +341,7 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(SampleArgs a) {
             const int n_eq_take = s_krem;          // elements equal to the threshold to keep
             const int n_gt = k - n_eq_take;        // elements strictly above it
             if (tid == 0) s_ngt = 0;
+            for (int i = tid; i < CMOLCU_TOPK_MAX; i += SMP_THREADS) { cval[i] = -1.0f; cidx[i] = -1; }
             __syncthreads();
             // strictly greater: unordered append (sorted below)
             for (int i = tid; i < V; i += SMP_THREADS) {
@@ -410,6 +421,10 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(SampleArgs a) {
         }
     }
     if (tid == 0) {
+        if (token < 0 || token >= V) {          // non-finite logits leave no valid candidate
+            if (a.fault) atomicExch(a.fault, FAULT_SAMPLE);
+            token = 0;
+        }
         a.out_ids[col] = token;
         if (!(st->eos >= 0 && token == st->eos)) {       // src/api.c:502-507
             st->ring[st->ring_head] = token;

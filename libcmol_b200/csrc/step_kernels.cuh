@@ -34,9 +34,12 @@ struct StepBeginArgs {
     StepMetaPtrs meta;
     int         *page_table;   // [slots][max_pages]
     int          max_pages;
+    int          max_slots;
+    int          n_pages;      // pages in the pool
     QWeight      embd;         // [vocab x d_model]
     float       *x;            // [B][d_model]
     int          d_model;
+    unsigned int *fault;       // device fault word
 };
 
 struct SampleArgs {
@@ -45,6 +48,7 @@ struct SampleArgs {
     int          vocab;
     SlotSampler *slots;
     int         *out_ids;      // [B]
+    unsigned int *fault;       // device fault word
 };
 
 // Per-head RMSNorm of q and k (optional attn_q_norm / attn_k_norm, shared

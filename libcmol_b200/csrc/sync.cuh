@@ -14,6 +14,9 @@ enum : unsigned int {
     FAULT_NONE = 0,
     FAULT_GEMV_FULL = 1,       // consumer waited too long for a stage
     FAULT_GEMV_EMPTY = 2,      // producer waited too long for a free stage
+    FAULT_BAD_TOKEN = 3,       // a token id outside [0, vocab) reached the embedding
+    FAULT_BAD_PAGE = 4,        // a page-table update outside the table / pool
+    FAULT_SAMPLE = 5,          // the sampler found no valid candidate (non-finite logits)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

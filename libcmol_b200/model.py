@@ -106,6 +106,8 @@ def api():
     sig("cmol_cuda_stats", C.c_int, [_vp, C.c_int, C.POINTER(CudaStats)])
     sig("cmol_cuda_stats_reset", None, [_vp])
     sig("cmol_cuda_n_gpus", C.c_int, [_vp])
+    sig("cmol_cuda_gemv_sweep", C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(C.c_double),
+                                          C.POINTER(C.c_longlong), C.POINTER(C.c_int)])
     _declared = True
     return L
 
@@ -163,6 +165,13 @@ class Model:
 
     def reset_stats(self):
         api().cmol_cuda_stats_reset(self.h)
+
+    def gemv_sweep(self, gpu: int = 0, reps: int = 20):
+        """(ms per pass, bytes per pass, launches per pass) of cmol_cuda_gemv_sweep."""
+        ms, nb, nl = C.c_double(0), C.c_longlong(0), C.c_int(0)
+        _chk(api().cmol_cuda_gemv_sweep(self.h, gpu, reps, C.byref(ms), C.byref(nb), C.byref(nl)),
+             "cmol_cuda_gemv_sweep")
+        return ms.value, nb.value, nl.value
 
     def encode(self, text: str, cap: int = 4096):
         out = np.zeros(cap, np.int32)

@@ -1,0 +1,191 @@
+"""End-to-end parity of the decode engine (libcmol.so public API) on a GPU.
+
+Checks, on the seeded synthetic GGUFs of tests/golden/:
+  * teacher-forced logits (cmol_forward_logits) against the reference's
+    cmol_model_forward logits: max-abs <= 2e-2 and cosine >= 0.9999 (the
+    tolerance the engine is specified to), and in practice far tighter;
+  * greedy token streams of cmol_generate_ids identical to the reference's
+    generate loop; sampled streams (top-k / top-p, seeded) identical as long
+    as no sampling decision falls within float rounding of a boundary;
+  * continuous batching: sessions generated together equal each alone;
+  * KV paging and split-context attention beyond one page / one split;
+  * stop rules and session bookkeeping (max_new, EOS, abort, reset).
+"""
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+MODELS = ["q8_0", "q5_0", "q4_k", "q6_k", "smollm3", "mixed"]
+ATOL, COS = 2e-2, 0.9999
+MODEL_KW = {
+    "q8_0": dict(dtype=8),
+    "smollm3": dict(dtype=12, n_layers=3, arch="smollm3", no_rope_interval=2, rope_base=5e6, qk_norm=True,
+                    tied=False, dt_head=8, n_heads=4, n_kv_heads=1),
+}
+
+
+def _mg():
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLD, "make_golden.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(os.path.join(GOLD, "models.npz"))
+
+
+@pytest.fixture(scope="module")
+def paths(tmp_path_factory):
+    d = tmp_path_factory.mktemp("gold")
+    mg = _mg()
+    return {n: mg.gguf_path(n, str(d)) for n in MODELS}
+
+
+def _cos(a, b):
+    return float(np.dot(a, b) / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def _params(tag):
+    from libcmol_b200.model import GenParams
+    return {"greedy": GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=20),
+            "greedy_pen": GenParams.make(0.0, repeat_penalty=1.3, repeat_last_n=8, max_new_tokens=20),
+            "topp": GenParams.make(0.9, top_p=0.9, top_k=40, seed=1234, repeat_penalty=1.1, max_new_tokens=20),
+            "topk": GenParams.make(1.2, top_p=1.0, top_k=5, seed=99, repeat_penalty=1.0, max_new_tokens=20)}[tag]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", MODELS)
+def test_teacher_forced_logits(gpu, golden, paths, name):
+    from libcmol_b200.model import Model
+    with Model(paths[name], max_ctx=64, max_sessions=2, page_tokens=4) as m:
+        s = m.acquire()
+        toks = golden[f"{name}_tokens"]
+        worst = 0.0
+        for i, t in enumerate(toks):
+            got = s.forward_logits(int(t))
+            ref = golden[f"{name}_logits"][i]
+            d = float(np.abs(got - ref).max())
+            worst = max(worst, d)
+            assert d <= ATOL and _cos(got, ref) >= COS, (i, d)
+        assert s.n_tokens == len(toks)
+        assert worst < 1e-3, worst          # f32 end to end: only summation order differs
+        s.release()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", MODELS)
+@pytest.mark.parametrize("tag", ["greedy", "greedy_pen", "topp", "topk"])
+def test_generate_matches_reference(gpu, golden, paths, name, tag):
+    from libcmol_b200.model import Model
+    with Model(paths[name], max_ctx=64, max_sessions=2) as m:
+        s = m.acquire()
+        rc, ids = s.generate_ids(golden[f"{name}_tokens"][:6], _params(tag))
+        assert rc == 0
+        assert ids == golden[f"{name}_gen_{tag}"].tolist()
+        # the prompt and every sampled token but the last (EOS or max_new) are in the KV cache
+        assert s.n_tokens == 6 + len(ids) - 1
+        s.release()
+
+
+@pytest.mark.gpu
+def test_continuous_batching_equals_single(gpu, paths):
+    from libcmol_b200.model import GenParams, Model
+    prompts = [[5, 6, 7], [100, 200, 300, 400, 500, 7, 8], [42], [9, 8, 7, 6, 5, 4, 3, 2, 1, 0, 11]]
+    params = [GenParams.make(0.0, max_new_tokens=12), GenParams.make(0.8, top_p=0.9, seed=5, max_new_tokens=9),
+              GenParams.make(0.0, repeat_penalty=1.2, max_new_tokens=15), GenParams.make(1.0, top_k=3, seed=7,
+                                                                                        max_new_tokens=10)]
+    with Model(paths["q4_k"], max_ctx=64, max_sessions=4, page_tokens=4) as m:
+        alone = []
+        for p, pa in zip(prompts, params):
+            s = m.acquire()
+            rc, ids = s.generate_ids(p, pa)
+            assert rc == 0
+            alone.append(ids)
+            s.release()
+        sess = [m.acquire() for _ in prompts]
+        together = m.generate_batch(sess, prompts, params)
+        assert [t.tolist() for t in together] == alone
+        for s in sess:
+            s.release()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "smollm3"])
+def test_long_context_pages_and_splits(gpu, tmp_path, name):
+    """300 tokens: many 16-token pages and three 128-token attention splits."""
+    from libcmol_b200 import synth
+    from libcmol_b200.model import Model
+    from oracle.oracle import OracleModel
+    kw = dict(MODEL_KW[name])
+    dt = kw.pop("dtype")
+    path = str(tmp_path / f"long_{name}.gguf")
+    synth.write_gguf(path, synth.tiny_spec(dt, ctx=512, **kw))
+    om = OracleModel(path, lanes=16)
+    os_ = om.session(512)
+    rng = np.random.default_rng(3)
+    toks = rng.integers(0, 512, size=300)
+    with Model(path, max_ctx=512, max_sessions=1) as m:
+        s = m.acquire()
+        for i, t in enumerate(toks):
+            got = s.forward_logits(int(t))
+            if i % 37 == 0 or i == len(toks) - 1:
+                ref = om.forward(os_, int(t), i)
+                assert np.abs(got - ref).max() <= ATOL and _cos(got, ref) >= COS, i
+            else:
+                om.forward(os_, int(t), i)
+        s.release()
+    om.free_session(os_)
+
+
+@pytest.mark.gpu
+def test_stop_rules_and_session_state(gpu, paths):
+    from libcmol_b200.model import GenParams, Model
+    with Model(paths["q8_0"], max_ctx=32, max_sessions=2) as m:
+        s = m.acquire()
+        # max_new: generated tokens are forwarded except the last one
+        rc, ids = s.generate_ids([5, 6, 7], GenParams.make(0.0, max_new_tokens=4))
+        assert rc == 0 and len(ids) == 4 and s.n_tokens == 3 + 3
+        # abort on the 2nd token: it is not forwarded, the call still returns OK
+        s.reset()
+        cnt = [0]
+
+        def stop_second(t, e):
+            cnt[0] += 1
+            return 1 if cnt[0] >= 2 else 0
+
+        rc, ids = s.generate_ids([5, 6, 7], GenParams.make(0.0, max_new_tokens=10), on_token=stop_second)
+        assert rc == 0 and cnt[0] == 2
+        assert s.n_tokens == 3 + 1
+        # context full: the loop stops at max_ctx, the next call reports it
+        s.reset()
+        rc, ids = s.generate_ids(list(range(20)), GenParams.make(0.0, max_new_tokens=-1))
+        assert rc == 0 and s.n_tokens == 32
+        rc, ids = s.generate_ids([1], GenParams.make(0.0))
+        assert rc == -7
+        s.release()
+        # pool: max_sessions slots, NULL when exhausted, fresh after release
+        a, b = m.acquire(), m.acquire()
+        assert a is not None and b is not None and m.acquire() is None
+        a.release()
+        c = m.acquire()
+        assert c is not None and c.n_tokens == 0
+        b.release()
+        c.release()
+
+
+
+@pytest.mark.gpu
+def test_text_generate_and_tokenizer(gpu, paths):
+    from libcmol_b200.model import GenParams, Model
+    with Model(paths["q8_0"], max_ctx=64, max_sessions=1) as m:
+        ids = m.encode("hello world")
+        assert len(ids) > 0
+        s = m.acquire()
+        rc, pieces = s.generate("hello world", GenParams.make(0.0, max_new_tokens=5))
+        assert rc == 0 and len(pieces) == 5
+        s.release()
