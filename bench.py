@@ -236,6 +236,7 @@ def main():
     ap.add_argument("--ref-steps", type=int, default=24)
     ap.add_argument("--ref-prompt", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -265,7 +266,10 @@ def main():
     from libcmol_b200 import synth
     from libcmol_b200.model import GenParams, Model
 
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.prompt > 0:
+        wl["prompt"] = args.prompt
+        wl["label"] += f" (prompt overridden to {args.prompt} tokens)"
     spec = synth.baseline_spec(wl["cfg"])
     path = ensure_model(spec, rank, barrier)
     ctx = wl["prompt"] + args.warmup + args.steps + 8

@@ -4,11 +4,12 @@
 // for every query head h of a session at position pos,
 //   out_h = sum_{t<=pos} softmax_t(q_h . k_t / sqrt(d_head)) v_t
 // with k/v of kv head h * n_kv / n_heads.  The context is split into chunks
-// of `split_tokens` (flash-decoding): CTA (split s, kv head, column) streams
-// its chunk of K and V pages once for all query heads of the group, keeps an
-// online softmax per head, and writes a partial (max, sum, acc[d_head]).  The
-// last CTA of a (column, kv head) to finish — found with an atomic counter —
-// merges the partials in split order (deterministic) and resets the counter.
+// of `split_tokens` (flash-decoding): CTA (split s, kv head, column) copies
+// the K and V blocks of its chunk's pages into shared memory with bulk
+// copies (once for all query heads of the group), scores every token of the
+// chunk, and writes a partial (max, sum, acc[d_head]) per head.  The last CTA
+// of a (column, kv head) to finish — found with an atomic counter — merges
+// the partials in split order (deterministic) and resets the counter.
 #pragma once
 #include "common.cuh"
 
@@ -37,5 +38,9 @@ struct AttnArgs {
 inline size_t attn_part_floats(int ncol, int n_heads, int n_splits, int d_head) {
     return (size_t)ncol * n_heads * n_splits * (d_head + 2);
 }
+
+// Dynamic shared memory one CTA needs (K and V tiles, queries, scores).
+size_t attention_smem_bytes(int d_head, int group, int split_tokens);
+#define CMOLCU_ATTN_SMEM_MAX (200 * 1024)
 
 cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl);

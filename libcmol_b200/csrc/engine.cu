@@ -143,6 +143,11 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     Engine *e = new Engine();
     e->device_ = device;
     e->opt_ = o;
+    // attention keeps a whole split of K and V in shared memory: shrink the
+    // split (in whole pages) until it fits
+    while (e->opt_.split_tokens > o.page_tokens &&
+           attention_smem_bytes(hd, hp.n_heads / nkv, e->opt_.split_tokens) > CMOLCU_ATTN_SMEM_MAX)
+        e->opt_.split_tokens -= o.page_tokens;
     e->vocab_ = V;
     Impl *d = new Impl();
     e->d = d;
@@ -243,7 +248,7 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     d->h = b.dalloc<float>((size_t)B * F);
     d->logits = b.dalloc<float>((size_t)B * V);
     d->qkvbuf = b.dalloc<float>((size_t)B * (D + 2 * KVD));
-    d->n_splits = (o.max_ctx + o.split_tokens - 1) / o.split_tokens;
+    d->n_splits = (o.max_ctx + e->opt_.split_tokens - 1) / e->opt_.split_tokens;
     d->part = b.dalloc<float>(attn_part_floats(B, hp.n_heads, d->n_splits, hd));
     d->counters = b.dalloc<int>((size_t)B * nkv);
 
