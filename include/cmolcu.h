@@ -92,6 +92,27 @@ int cmolcu_gemv_bench(cmolcu_weight_t *const *ws, int nw, const float *x, int n,
 void cmolcu_matmul(float *out, const void *a, const float *b,
                    int m, int k, int n, int dtype);
 
+/* ---- the matmul seam without device allocation -----------------------------
+ * No counterpart in the reference (its matmul never touches a device).
+ * cmolcu_matmul, same signature and results, but it allocates no device
+ * memory: no cudaMalloc/cudaFree or other allocating call.  It is for callers
+ * that cannot allocate: code running beside a live decode engine (cudaFree
+ * waits for the whole device and would stall its streams) or under a memory
+ * pool that already holds the free memory.  All working memory lives in one
+ * static device array of CMOLCU_NOALLOC_SCRATCH_BYTES per device:
+ *   256 + up256(m * row_bytes(k)) + up256(repacked planes of A)
+ *       + up256(4*k*n) + up256(4*m*n)       must be <= the limit
+ * (up256 = round up to 256; e.g. 11008 x 2048 Q8_0 fits up to n = 128).
+ * Larger requests are rejected: out untouched, cmolcu_last_error() says so.
+ * cmolcu_last_error() is "" after a call that succeeded.
+ * The first call on each device looks up the scratch address and sets the
+ * GEMV's shared-memory attribute; make it before any stream capture.
+ * Calls on one device share the scratch: overlapping calls (two threads at
+ * once) race and must be serialised by the caller. */
+#define CMOLCU_NOALLOC_SCRATCH_BYTES (64u << 20)
+void cmolcu_matmul_noalloc(float *out, const void *a, const float *b,
+                           int m, int k, int n, int dtype);
+
 /* ---- host-only tokenizer -------------------------------------------------
  * The vocabulary of a GGUF file without loading weights or using a GPU:
  * the same encoder and decoder cmol_encode / cmol_decode_token use
