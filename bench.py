@@ -6,7 +6,7 @@ random prompt, greedy decoding.  A "step" is one decode step: one token per
 session through all 32 layers, the LM head and the sampler.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c2|c3|c5]
+                    [--workload c1|c2|c5]
 
 Multi-GPU runs are launched with torch.distributed.run, one process per GPU;
 sessions are independent (weights replicated, no collective on the data
@@ -41,7 +41,55 @@ WORKLOADS = {
                                         "128-token random prompt, greedy decode"),
     "c1": dict(cfg=1, prompt=32, label="config1: SmolLM2-135M-shape, GGUF Q8_0, 1 session per GPU, "
                                        "32-token random prompt, greedy decode"),
+    "c5": dict(cfg=5, prompt=0, label="config5: dequant-dot GEMV microbench, 11008x2048 seeded N(0,0.02) "
+                                      "weights block-quantised, f32 activations, back-to-back launches over "
+                                      "distinct weight copies totalling > 2x L2"),
 }
+
+GEMV_M, GEMV_K = 11008, 2048
+
+
+def run_gemv_microbench(args, rank, local):
+    """Config 5: device time per GEMV for each format and column count, over
+    back-to-back launches (one CUDA graph) rotating over distinct copies of
+    the weight whose total exceeds twice the L2, so every launch streams
+    from HBM.  value = Q4_K at n=1 in GB/s of GGUF bytes."""
+    import numpy as np
+    import torch
+
+    from libcmol_b200 import Weight, gemv_bench, synth
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    peak, peak_kind = peaks()
+    res = {}
+    for dt in (synth.Q4_K, synth.Q8_0, synth.Q4_0, synth.Q5_0, synth.Q6_K):
+        rng = np.random.default_rng(0)
+        blob = synth.quantize(rng.standard_normal((GEMV_M, GEMV_K), dtype=np.float32) * 0.02, dt)
+        nbytes = int(blob.nbytes)
+        ncopy = max(2, int(2 * 2 * 126e6 // nbytes) + 1)
+        ws = [Weight(blob, dt, GEMV_M, GEMV_K) for _ in range(ncopy)]
+        row = {}
+        for n in (1, 2):
+            x = torch.randn(n, GEMV_K, device=f"cuda:{local}")
+            y = torch.zeros(n, GEMV_M, device=f"cuda:{local}")
+            gemv_bench(ws, x, y, n, iters=2 * ncopy, reps=2)              # warm-up
+            ms = gemv_bench(ws, x, y, n, iters=4 * ncopy, reps=max(3, args.steps // 16))
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            row[str(n)] = {"us": round(ms * 1e3, 3), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        res[synth.DTYPE_NAMES[dt]] = {"bytes": nbytes, "copies": ncopy, "n": row}
+        for w in ws:
+            w.free()
+    v = res["Q4_K"]["n"]["1"]
+    print(json.dumps({
+        "metric": "GEMV HBM GB/s (11008x2048 dequant-dot, n=1, Q4_K)", "value": v["GBps"], "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v["us"] / 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOADS["c5"]["label"], "l2": "weight copies rotate over > 2x L2"},
+        "roofline": {"bound": "hbm", "achieved": v["GBps"], "peak": peak, "unit": "GB/s",
+                     "frac": round(v["GBps"] / peak, 4), "traffic": None, "peak_source": peak_kind},
+        "sweep": res,
+    }), flush=True)
 
 
 def env_int(name, default):
@@ -257,6 +305,11 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    if args.workload == "c5":
+        run_gemv_microbench(args, rank, local)
         if dist is not None:
             dist.destroy_process_group()
         return

@@ -253,8 +253,8 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
             eo.page_tokens = opt.kv_page_tokens > 0 ? opt.kv_page_tokens : 16;
             eo.kv_pool_frac = opt.kv_pool_frac > 0.f ? opt.kv_pool_frac : 0.85f;
             eo.use_graphs = opt.use_graphs != 0;
-            eo.split_tokens = 128;
-            if (eo.split_tokens % eo.page_tokens) eo.split_tokens = eo.page_tokens * 8;
+            eo.split_tokens = 64;
+            if (eo.split_tokens % eo.page_tokens) eo.split_tokens = eo.page_tokens * 4;
             char msg[256] = {0};
             int e = 0;
             Engine *en = Engine::create(devs[g], m->host, eo, &e, msg, sizeof msg);

@@ -1,0 +1,205 @@
+// attention_item.cuh — one work item of split-context GQA decode attention,
+// shared by the standalone kernel (attention.cu) and the persistent decode
+// step kernel (decode_step.cu).
+//
+// Item = (context split s, kv head hk, column col), run by ATTN_THREADS
+// threads that synchronise on named barrier 1.  Thread 0 moves the K and V
+// blocks of the split's pages (each a contiguous page_tokens x d_head block
+// in the page layout) into shared memory with cp.async.bulk on one mbarrier
+// while the others load the G = n_heads / n_kv queries.  Scores: one thread
+// per (token, head).  Softmax per head.  P.V: (head, float4 of d_head) items
+// with the split's tokens divided among thread groups.  The partial (max,
+// sum, acc) goes to a.part; the last item of a (column, kv head) to finish —
+// found with an atomic counter — merges the partials in split order (so the
+// result does not depend on scheduling) and resets the counter.
+// Replaces step 5 of cmol_attn_forward (src/attn.c:103-137).
+#pragma once
+#include "attention.cuh"
+#include "sync.cuh"
+
+#define ATTN_WARPS 8
+#define ATTN_THREADS (ATTN_WARPS * 32)
+#define ATTN_MAX_G 8
+
+struct AttnShared {
+    float wsum[ATTN_MAX_G], wmax[ATTN_MAX_G];
+    int   last, ok;
+};
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Shared-memory floats of one item (K and V tiles, queries, scores, P.V sums).
+__host__ __device__ inline size_t attn_item_smem_bytes(int d_head, int G, int split_tokens) {
+    return (size_t)2 * split_tokens * d_head * 4 + (size_t)G * d_head * 4 + (size_t)G * split_tokens * 4 +
+           (size_t)ATTN_THREADS * 16;
+}
+
+// `sm` is 16-byte aligned; `bar` an initialised mbarrier (count 1) whose
+// next phase has parity `parity` (toggled here when the item waits on it).
+// Returns false when a wait ran out (fault word set); every thread returns
+// the same value at the same point.
+// `pos` is the column's position (< 0: inactive) and `pt` its page-table row
+// (global or shared memory).
+template <int E>
+__device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, const int *pt, float *sm,
+                          uint64_t *bar, uint32_t &parity, AttnShared &sh, int tid) {
+    constexpr int hd = 32 * E, HD4 = hd / 4;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int G = a.n_heads / a.n_kv;
+    const int S = a.split_tokens;
+    const int P = a.page_tokens;
+
+    float *Ks = sm;                              // [S][hd]
+    float *Vs = Ks + (size_t)S * hd;             // [S][hd]
+    float *Qs = Vs + (size_t)S * hd;             // [G][hd]
+    float *Sc = Qs + (size_t)G * hd;             // [G][S]
+    float4 *Red = reinterpret_cast<float4 *>(Sc + (size_t)G * S);   // [ATTN_THREADS]
+
+    if (pos < 0) return true;
+    const int t0 = s * S;
+    if (t0 > pos) return true;
+    const int n = min(S, pos + 1 - t0);                       // tokens in this split
+    const int n_active = (pos + S) / S;
+    const long long head_off = ((long long)a.layer * 2 * a.n_kv + hk) * P * hd;   // K block in a page
+    const long long v_off = (long long)a.n_kv * P * hd;                            // V block follows
+
+    if (tid == 0) {
+        int ok = 1;
+        const int npg = (n + P - 1) / P;
+        for (int i = 0; i < npg; i++) {
+            int pg = pt[t0 / P + i];
+            if (pg < 0 || pg >= a.n_pages) ok = 0;
+        }
+        if (ok) {
+            // the KV rows of this step were written through the generic proxy
+            fence_proxy_async_global();
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * npg * P * hd * 4));
+            for (int i = 0; i < npg; i++) {
+                const float *kp = a.kv_pages + (long long)pt[t0 / P + i] * a.page_floats + head_off;
+                bulk_g2s(Ks + (size_t)i * P * hd, kp, (uint32_t)(P * hd * 4), bar);
+                bulk_g2s(Vs + (size_t)i * P * hd, kp + v_off, (uint32_t)(P * hd * 4), bar);
+            }
+        } else if (a.fault) {
+            atomicExch(a.fault, FAULT_BAD_PAGE);
+        }
+        sh.ok = ok;
+    }
+    for (int i = tid; i < G * hd; i += ATTN_THREADS)
+        Qs[i] = __ldcg(a.q + (long long)col * a.q_ld + (long long)hk * G * hd + i);
+    named_bar_sync(1, ATTN_THREADS);
+    if (!sh.ok) return false;
+    const bool got = mbar_wait(bar, parity, a.fault, FAULT_ATTN_WAIT);
+    parity ^= 1u;
+    if (!got) sh.ok = 0;
+    named_bar_sync(1, ATTN_THREADS);
+    if (!sh.ok) return false;
+
+    // scores: one thread per (token, head).  Lane l starts its walk over the
+    // row at float4 l % HD4, so the 8 lanes of a shared-memory phase touch 8
+    // different 16-byte bank groups of their (different) K rows.
+    {
+        const float4 *K4 = reinterpret_cast<const float4 *>(Ks);
+        const float4 *Q4 = reinterpret_cast<const float4 *>(Qs);
+        for (int w = tid; w < n * G; w += ATTN_THREADS) {
+            const int t = w % n, g = w / n;
+            const float4 *kr = K4 + (size_t)t * HD4;
+            const float4 *qr = Q4 + (size_t)g * HD4;
+            float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < HD4; j++) {
+                const int c = (j + lane) & (HD4 - 1);
+                const float4 k = kr[c], q = qr[c];
+                d0 = __fmaf_rn(q.x, k.x, d0);
+                d1 = __fmaf_rn(q.y, k.y, d1);
+                d0 = __fmaf_rn(q.z, k.z, d0);
+                d1 = __fmaf_rn(q.w, k.w, d1);
+            }
+            Sc[g * S + t] = (d0 + d1) * a.scale;
+        }
+    }
+    named_bar_sync(1, ATTN_THREADS);
+    // per-head softmax over the split (max, exp, sum)
+    for (int g = warp; g < G; g += ATTN_WARPS) {
+        float m = -INFINITY;
+        for (int t = lane; t < n; t += 32) m = fmaxf(m, Sc[g * S + t]);
+        m = warp_max(m);
+        float sum = 0.f;
+        for (int t = lane; t < n; t += 32) {
+            float e = expf(Sc[g * S + t] - m);
+            Sc[g * S + t] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) { sh.wmax[g] = m; sh.wsum[g] = sum; }
+    }
+    named_bar_sync(1, ATTN_THREADS);
+    // P.V: item = (head, float4 of d_head); the split's tokens are divided
+    // among `parts` thread groups whose float4 sums meet in shared memory.
+    {
+        const int items = G * HD4;
+        const int parts = max(1, min(ATTN_THREADS / items, n));
+        const int item = tid % items, part = tid / items;
+        if (part < parts) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            const int g = item / HD4, c = item % HD4;
+            const float *p = Sc + g * S;
+            const float4 *V4 = reinterpret_cast<const float4 *>(Vs) + c;
+            const int tb = (int)((long long)n * part / parts), te = (int)((long long)n * (part + 1) / parts);
+            for (int t = tb; t < te; t++) {
+                const float pt_ = p[t];
+                const float4 v = V4[(size_t)t * HD4];
+                acc.x = __fmaf_rn(pt_, v.x, acc.x);
+                acc.y = __fmaf_rn(pt_, v.y, acc.y);
+                acc.z = __fmaf_rn(pt_, v.z, acc.z);
+                acc.w = __fmaf_rn(pt_, v.w, acc.w);
+            }
+            Red[tid] = acc;
+        }
+        named_bar_sync(1, ATTN_THREADS);
+        for (int i = tid; i < items; i += ATTN_THREADS) {
+            float4 r = Red[i];
+            for (int q = 1; q < parts; q++) {
+                const float4 o = Red[q * items + i];
+                r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
+            }
+            const int g = i / HD4, c = i % HD4;
+            float *pp = a.part + (((long long)col * a.n_heads + hk * G + g) * a.n_splits + s) * (hd + 2);
+            pp[4 * c + 0] = r.x;
+            pp[4 * c + 1] = r.y;
+            pp[4 * c + 2] = r.z;
+            pp[4 * c + 3] = r.w;
+            if (c == 0) { pp[hd] = sh.wmax[g]; pp[hd + 1] = sh.wsum[g]; }
+        }
+    }
+    __threadfence();
+    named_bar_sync(1, ATTN_THREADS);
+    if (tid == 0) {
+        int old = atomicAdd(&a.counters[col * a.n_kv + hk], 1);
+        sh.last = (old == n_active - 1);
+    }
+    named_bar_sync(1, ATTN_THREADS);
+    if (!sh.last) return true;
+    __threadfence();
+
+    // last item of (column, kv head): merge the splits in order
+    for (int i = tid; i < G * hd; i += ATTN_THREADS) {
+        const int g = i / hd, d = i % hd;
+        const float *base = a.part + ((long long)col * a.n_heads + hk * G + g) * a.n_splits * (hd + 2);
+        float M = -INFINITY;
+        for (int sp = 0; sp < n_active; sp++) M = fmaxf(M, __ldcg(base + sp * (hd + 2) + hd));
+        float L = 0.f, A = 0.f;
+        for (int sp = 0; sp < n_active; sp++) {
+            const float *pp = base + sp * (hd + 2);
+            const float f = expf(__ldcg(pp + hd) - M);
+            L = __fmaf_rn(__ldcg(pp + hd + 1), f, L);
+            A = __fmaf_rn(__ldcg(pp + d), f, A);
+        }
+        a.out[(long long)col * a.out_ld + (long long)(hk * G + g) * hd + d] = A / L;
+    }
+    if (tid == 0) a.counters[col * a.n_kv + hk] = 0;
+    // the Red / Sc buffers are reused by the next item
+    named_bar_sync(1, ATTN_THREADS);
+    return true;
+}

@@ -22,7 +22,7 @@ struct EngineOptions {
     int   page_tokens = 16;
     float kv_pool_frac = 0.85f;
     bool  use_graphs = true;
-    int   split_tokens = 128;  // attention context split
+    int   split_tokens = 64;   // attention context split (tokens per work item)
 };
 
 struct SamplerParams {
@@ -65,6 +65,8 @@ class Engine {
     int  page_tokens() const { return opt_.page_tokens; }
     int  max_pages_per_slot() const { return max_pages_; }
     int  max_batch() const { return opt_.max_batch; }
+    int  max_pages() const { return max_pages_; }
+    const EngineOptions &options() const { return opt_; }
     int  vocab() const { return vocab_; }
     long long weight_bytes_per_step() const { return weight_bytes_; }
     long long kv_bytes_per_token() const { return kv_bytes_per_token_; }

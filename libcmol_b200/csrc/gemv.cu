@@ -147,9 +147,11 @@ static void fmt_of(int dt, int &vpc, int &cr) {
 
 // Choose rows per warp, rows per CTA, K-chunk and pipeline depth for one
 // launch.  Every CTA gets one contiguous range of rows (a multiple of R), so
-// the work of an SM is balanced to a few rows.  A CTA first tries to stay
-// under ~100 KB of shared memory (two CTAs per SM, so the next kernel of the
-// step can start streaming while this one drains).
+// the work of an SM is balanced to a few rows.  Small matrices (the decode
+// step's) use two CTAs per SM of up to ~100 KB of shared memory each, so the
+// next kernel of the step can start streaming while this one drains.  Large
+// matrices use one CTA per SM with up to ~216 KB, so an SM's whole share (or
+// most of it) is in flight at once.
 bool gemv_plan(const QWeight &w, int nc, PipeCfg &pc, int &R, int &grid) {
     const int sms = device_sm_count();
     R = 4;
@@ -163,7 +165,9 @@ bool gemv_plan(const QWeight &w, int nc, PipeCfg &pc, int &R, int &grid) {
         off += p < w.nplanes ? tr * w.cs[p] : 0;
     }
     pc.sb = off;
-    for (int budget_kb : {100, 216}) {
+    const bool large = w.bytes >= (size_t)4 << 20;
+    const int order[2][2] = {{100, 216}, {216, 100}};
+    for (int budget_kb : order[large ? 1 : 0]) {
         const long long avail = (long long)budget_kb * 1024 - (long long)xb - 2 * GEMV_MAX_STAGES * 8;
         if (avail < 2LL * pc.sb) continue;
         const int ctas = sms * (budget_kb <= 100 ? 2 : 1);

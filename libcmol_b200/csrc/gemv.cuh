@@ -74,7 +74,7 @@ struct GemvArgs {
 
 #define GEMV_CWARPS 8                          // consumer warps
 #define GEMV_THREADS ((GEMV_CWARPS + 1) * 32)  // + one producer warp
-#define GEMV_MAX_STAGES 8
+#define GEMV_MAX_STAGES 16
 
 static constexpr float kXScale    = 38685626227668133590597632.0f;  // 2^85
 static constexpr float kQScaleInv = 18446744073709551616.0f;        // 2^64
@@ -253,7 +253,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const
             if (row < rows && col < a.ncol) {
                 float *p = a.y + (long long)col * a.y_ld + (long long)row * a.y_inc;
                 float v = vals[lane];
-                if constexpr (EPI == EPI_RESID) *p = *p + v;   // x += sublayer out (src/model.c:232,259)
+                if constexpr (EPI == EPI_RESID) *p = __ldcg(p) + v;   // x += sublayer out (src/model.c:232,259)
                 else *p = v;
             }
         }

@@ -88,12 +88,26 @@ __host__ __device__ inline uint8_t *qw_row(const QWeight &w, int p, int j, long 
 }
 
 // Default K-chunk: the whole row when 32 rows of it stay near 24 KB,
-// otherwise the largest multiple of the block size that does.
+// otherwise the largest multiple of 32 payload chunks (512 values for the
+// 16-value-chunk formats Q8_0/F16/F32, 1024 for the others) that does, so
+// every lane of a warp walking a K-chunk has work; the largest multiple of
+// the block size when not even one such unit fits.
 __host__ inline int qw_default_kc(int dt, int k) {
     const int bv = dt_block_values(dt);
     int per32 = 0;
     for (int p = 0; p < qw_nplanes(dt); p++) per32 += round16(qw_plane_bytes(dt, p, k));
     if (32 * per32 <= 24 * 1024 || bv <= 0) return k;
+    const int unit = (dt == DT_Q8_0 || dt == DT_F16 || dt == DT_F32) ? 512 : 1024;
+    auto fits = [&](int kc) {
+        int b = 0;
+        for (int p = 0; p < qw_nplanes(dt); p++) b += round16(qw_plane_bytes(dt, p, kc));
+        return 32 * b <= 24 * 1024;
+    };
+    if (unit % bv == 0 && fits(unit)) {
+        int kc = unit;
+        while (kc + unit < k && fits(kc + unit)) kc += unit;
+        return kc;
+    }
     // bytes per value (all planes) ~ per32 / k
     long long kc = (long long)24 * 1024 * k / (32LL * per32);
     kc = kc / bv * bv;

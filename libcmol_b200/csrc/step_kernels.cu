@@ -61,6 +61,7 @@ __global__ void k_step_begin(StepBeginArgs a) {
     pdl_launch_dependents();
     const int col = blockIdx.x;
     if (col == 0) {
+        if (threadIdx.x == 0 && a.sync_reset) *a.sync_reset = 0u;
         const int n = *a.meta.n_upd;
         for (int u = threadIdx.x; u < n; u += blockDim.x) {
             int s = a.meta.upd[3 * u], idx = a.meta.upd[3 * u + 1], pg = a.meta.upd[3 * u + 2];
