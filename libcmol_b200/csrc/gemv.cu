@@ -83,32 +83,33 @@ int device_sm_count() {
 // ---------------------------------------------------------------------------
 typedef void (*gemv_kernel_t)(GemvArgs);
 
-template <int DT, int NC, int R>
+template <int DT, int NC, int R, int CW>
 static gemv_kernel_t pick_epi(int epi) {
     switch (epi) {
-    case EPI_STORE:  return k_gemv<DT, NC, R, EPI_STORE>;
-    case EPI_RESID:  return k_gemv<DT, NC, R, EPI_RESID>;
-    case EPI_SWIGLU: return k_gemv<DT, NC, R, EPI_SWIGLU>;
-    case EPI_QKV:    return k_gemv<DT, NC, R, EPI_QKV>;
+    case EPI_STORE:  return k_gemv<DT, NC, R, EPI_STORE, CW>;
+    case EPI_RESID:  return k_gemv<DT, NC, R, EPI_RESID, CW>;
+    case EPI_SWIGLU: return k_gemv<DT, NC, R, EPI_SWIGLU, CW>;
+    case EPI_QKV:    return k_gemv<DT, NC, R, EPI_QKV, CW>;
     default: return nullptr;
     }
 }
 
 template <int DT>
-static gemv_kernel_t pick_dt(int nc, int r, int epi) {
+static gemv_kernel_t pick_dt(int nc, int r, int epi, int cw) {
     if (r != 4) return nullptr;
-    return nc == 1 ? pick_epi<DT, 1, 4>(epi) : pick_epi<DT, 2, 4>(epi);
+    if (cw == GEMV_CWARPS_WIDE) return nc == 1 ? pick_epi<DT, 1, 4, GEMV_CWARPS_WIDE>(epi) : pick_epi<DT, 2, 4, GEMV_CWARPS_WIDE>(epi);
+    return nc == 1 ? pick_epi<DT, 1, 4, GEMV_CWARPS>(epi) : pick_epi<DT, 2, 4, GEMV_CWARPS>(epi);
 }
 
-static gemv_kernel_t pick(int dt, int nc, int r, int epi) {
+static gemv_kernel_t pick(int dt, int nc, int r, int epi, int cw) {
     switch (dt) {
-    case DT_Q8_0: return pick_dt<DT_Q8_0>(nc, r, epi);
-    case DT_Q4_0: return pick_dt<DT_Q4_0>(nc, r, epi);
-    case DT_Q5_0: return pick_dt<DT_Q5_0>(nc, r, epi);
-    case DT_Q4_K: return pick_dt<DT_Q4_K>(nc, r, epi);
-    case DT_Q6_K: return pick_dt<DT_Q6_K>(nc, r, epi);
-    case DT_F16:  return pick_dt<DT_F16>(nc, r, epi);
-    case DT_F32:  return pick_dt<DT_F32>(nc, r, epi);
+    case DT_Q8_0: return pick_dt<DT_Q8_0>(nc, r, epi, cw);
+    case DT_Q4_0: return pick_dt<DT_Q4_0>(nc, r, epi, cw);
+    case DT_Q5_0: return pick_dt<DT_Q5_0>(nc, r, epi, cw);
+    case DT_Q4_K: return pick_dt<DT_Q4_K>(nc, r, epi, cw);
+    case DT_Q6_K: return pick_dt<DT_Q6_K>(nc, r, epi, cw);
+    case DT_F16:  return pick_dt<DT_F16>(nc, r, epi, cw);
+    case DT_F32:  return pick_dt<DT_F32>(nc, r, epi, cw);
     default: return nullptr;
     }
 }
@@ -155,19 +156,22 @@ static void fmt_of(int dt, int &vpc, int &cr) {
 bool gemv_plan(const QWeight &w, int nc, PipeCfg &pc, int &R, int &grid) {
     const int sms = device_sm_count();
     R = 4;
-    const int tr = 8 * R;
     int vpc, cr;
     fmt_of(w.dtype, vpc, cr);
     const size_t xb = gemv_x_bytes(nc, w.k, vpc, cr);
-    int off = 0;
-    for (int p = 0; p < 4; p++) {
-        pc.po[p] = off;
-        off += p < w.nplanes ? tr * w.cs[p] : 0;
-    }
-    pc.sb = off;
     const bool large = w.bytes >= (size_t)4 << 20;
     const int order[2][2] = {{100, 216}, {216, 100}};
     for (int budget_kb : order[large ? 1 : 0]) {
+        // one CTA per SM gets the wide variant (15 consumer warps)
+        const int cw = budget_kb <= 100 ? GEMV_CWARPS : GEMV_CWARPS_WIDE;
+        const int tr = cw * R;
+        int off = 0;
+        for (int p = 0; p < 4; p++) {
+            pc.po[p] = off;
+            off += p < w.nplanes ? tr * w.cs[p] : 0;
+        }
+        pc.sb = off;
+        pc.cw = cw;
         const long long avail = (long long)budget_kb * 1024 - (long long)xb - 2 * GEMV_MAX_STAGES * 8;
         if (avail < 2LL * pc.sb) continue;
         const int ctas = sms * (budget_kb <= 100 ? 2 : 1);
@@ -193,14 +197,14 @@ cudaError_t gemv_launch(const GemvArgs &a0, int epi, cudaStream_t st, bool pdl) 
     if (a.norm_w && ((uintptr_t)a.norm_w & 15)) return cudaErrorMisalignedAddress;
     int R = 4, grid = 1;
     if (!gemv_plan(a.w, a.ncol, a.pc, R, grid)) return cudaErrorInvalidValue;
-    gemv_kernel_t k = pick(a.w.dtype, a.ncol, R, epi);
+    gemv_kernel_t k = pick(a.w.dtype, a.ncol, R, epi, a.pc.cw);
     if (!k) return cudaErrorInvalidValue;
     const size_t lim = ensure_smem_attr(k);
     int vpc, cr;
     fmt_of(a.w.dtype, vpc, cr);
     size_t smem = gemv_smem_total(a.ncol, a.w.k, vpc, cr, a.pc);
     if (smem > lim) return cudaErrorInvalidConfiguration;
-    return launch_k(k, dim3(grid), dim3(GEMV_THREADS), smem, st, pdl, a);
+    return launch_k(k, dim3(grid), dim3((a.pc.cw + 1) * 32), smem, st, pdl, a);
 }
 
 cudaError_t gemv_launch_cols(GemvArgs a, int ncol, int epi, cudaStream_t st, bool pdl) {

@@ -7,19 +7,23 @@
 //   xn = w[k] * (x[k] * inv_rms) otherwise (RMSNorm of src/model.c:90-97,
 //                                fused into the prologue)
 //
-// Data movement.  A CTA owns row tiles of TR = 8*R rows (round robin over
-// the grid).  A tile moves in K-chunks of KC values (KC = k unless a tile
-// would not fit a few pipeline stages).  One producer warp copies each
-// (tile, K-chunk) into a shared-memory stage with cp.async.bulk — lane r
-// copies row r of every plane — and the stage's "full" mbarrier completes
-// on the transaction byte count.  A CTA's whole share of a small matrix is
-// in flight as soon as the kernel starts; weights do not depend on the
-// previous kernel, so the producer never waits for it (programmatic
-// dependent launch).  Eight consumer warps stage the activations, then each
-// takes R rows of the tile: lane l owns 16-byte payload chunks l, l+32, ...
-// of the K-chunk, loads a chunk's activations from shared memory once and
-// reuses them for its R rows.  Consumers release a stage through its
-// "empty" mbarrier.  Every wait is bounded (sync.cuh).
+// Data movement.  A CTA owns one contiguous range of rows, walked in tiles
+// of TR = CW*R rows (CW consumer warps, R rows each).  A tile moves in
+// K-chunks of KC values (qweight.cuh: the whole row, or a multiple of 32
+// payload chunks that keeps 32 rows near 24 KB).  One lane of the producer
+// warp copies each (tile, K-chunk) into a shared-memory stage with one
+// cp.async.bulk per plane — the rows of a K-chunk are contiguous in the
+// K-chunk-major layout — and the stage's "full" mbarrier completes on the
+// transaction byte count.  Weights do not depend on the previous kernel, so
+// the producer never waits for it (programmatic dependent launch).  The
+// consumer warps stage the activations, then each takes R rows of the tile:
+// lane l owns 16-byte payload chunks l, l+32, ... of the K-chunk, loads a
+// chunk's activations from shared memory once and reuses them for its R
+// rows.  Consumers release a stage through its "empty" mbarrier.  Every wait
+// is bounded (sync.cuh).  Two variants: CW = 8 (two CTAs an SM, ~100 KB of
+// shared memory each: small decode matrices, so the next kernel streams
+// while this one drains) and CW = 15 (one CTA an SM, up to ~216 KB: large
+// matrices, more warps to issue the dequant arithmetic).
 //
 // Integer -> float without I2F.  A quantised value q (0..255 after biasing)
 // placed in the low bits of a 32-bit word is the float q * 2^-149 (a
@@ -59,6 +63,7 @@ struct PipeCfg {
     int sb;          // stage bytes
     int nstage;      // pipeline depth
     int rows_per_cta;// contiguous rows per CTA (multiple of R)
+    int cw;          // consumer warps (GEMV_CWARPS or GEMV_CWARPS_WIDE); a stage holds cw * R rows
 };
 
 struct GemvArgs {
@@ -72,8 +77,9 @@ struct GemvArgs {
     unsigned int *fault;                             // device fault word (may be NULL)
 };
 
-#define GEMV_CWARPS 8                          // consumer warps
+#define GEMV_CWARPS 8                          // consumer warps of the small-matrix variant
 #define GEMV_THREADS ((GEMV_CWARPS + 1) * 32)  // + one producer warp
+#define GEMV_CWARPS_WIDE 15                    // consumer warps of the large-matrix variant (16 warps in all: 128 registers a thread)
 #define GEMV_MAX_STAGES 16
 
 static constexpr float kXScale    = 38685626227668133590597632.0f;  // 2^85
@@ -129,12 +135,26 @@ __device__ __forceinline__ void chunk_runs(int c, int &r0, int &r1) {
     }
 }
 
-// Q4_K 6-bit scale and min of sub-block j from the 12 packed bytes
-// (src/quant.c:125-134).  sb[0..2] hold bytes 0-3, 4-7, 8-11.
-__device__ __forceinline__ void q4k_sm(const uint32_t sb[3], int j, int &sc, int &mn) {
-    auto byte = [&](int i) -> int { return (int)((sb[i >> 2] >> (8 * (i & 3))) & 0xFFu); };
-    if (j < 4) { sc = byte(j) & 63; mn = byte(j + 4) & 63; }
-    else { sc = (byte(j + 4) & 15) | ((byte(j - 4) >> 6) << 4); mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4); }
+// Q4_K 6-bit scales and mins of the sub-block pair (2j, 2j+1) of a
+// super-block, from its 12 packed bytes (src/quant.c:125-134) in three
+// words w0 (bytes 0-3), w1 (4-7), w2 (8-11).  For j < 2 the pair is bytes
+// 2j, 2j+1 of w0 (scales) and w1 (mins), low 6 bits; for j >= 2 the low
+// 4 bits come from w2 (scales: low nibbles, mins: high nibbles) and the top
+// 2 bits from bits 6-7 of the corresponding bytes of w0 / w1.  Both bytes
+// of a pair are extracted at once; j is the same for every chunk a lane
+// handles, so the selects below are loop invariant.
+__device__ __forceinline__ void q4k_pair(uint32_t w0, uint32_t w1, uint32_t w2, int j, float &sc0, float &sc1,
+                                         float &mn0, float &mn1) {
+    const int h = (j & 1) * 16;
+    const bool hi = j >= 2;
+    const uint32_t mlo = hi ? 0x0F0Fu : 0x3F3Fu, mhi = hi ? 0x3030u : 0u;
+    const uint32_t sp = (((hi ? w2 : w0) >> h) & mlo) | (((w0 >> h) >> 2) & mhi);
+    const uint32_t mp = (((hi ? (w2 >> 4) : w1) >> h) & mlo) | (((w1 >> h) >> 2) & mhi);
+    // small integers to float without a conversion instruction: 2^23 + v
+    sc0 = __uint_as_float(0x4B000000u | (sp & 0xFFu)) - 8388608.0f;
+    sc1 = __uint_as_float(0x4B000000u | ((sp >> 8) & 0xFFu)) - 8388608.0f;
+    mn0 = __uint_as_float(0x4B000000u | (mp & 0xFFu)) - 8388608.0f;
+    mn1 = __uint_as_float(0x4B000000u | ((mp >> 8) & 0xFFu)) - 8388608.0f;
 }
 
 // Contribution of local chunk cl (global chunk c) of stage row `tr`
@@ -176,18 +196,15 @@ __device__ __forceinline__ float chunk_math(const uint8_t *stage, const PipeCfg 
         const uint4 h = *reinterpret_cast<const uint4 *>(P1 + (cl >> 3) * 16);
         float d    = h2f((uint16_t)(h.x & 0xFFFF));
         float dmin = h2f((uint16_t)(h.x >> 16));
-        uint32_t sb[3] = {h.y, h.z, h.w};
-        int j = (c & 7) >> 1;
-        int sc0, mn0, sc1, mn1;
-        q4k_sm(sb, 2 * j, sc0, mn0);
-        q4k_sm(sb, 2 * j + 1, sc1, mn1);
+        float sc0, sc1, mn0, mn1;
+        q4k_pair(h.y, h.z, h.w, (c & 7) >> 1, sc0, sc1, mn0, mn1);
         uint32_t lo[4] = {pl.x & 0x0F0F0F0Fu, pl.y & 0x0F0F0F0Fu, pl.z & 0x0F0F0F0Fu, pl.w & 0x0F0F0F0Fu};
         uint32_t hi[4] = {(pl.x >> 4) & 0x0F0F0F0Fu, (pl.y >> 4) & 0x0F0F0F0Fu,
                           (pl.z >> 4) & 0x0F0F0F0Fu, (pl.w >> 4) & 0x0F0F0F0Fu};
         float a0 = dot_run16(lo, x0);
         float a1 = dot_run16(hi, x1);
-        float db0 = d * (float)sc0, mb0 = dmin * (float)mn0;
-        float db1 = d * (float)sc1, mb1 = dmin * (float)mn1;
+        float db0 = d * sc0, mb0 = dmin * mn0;
+        float db1 = d * sc1, mb1 = dmin * mn1;
         return __fmaf_rn(db0, a0, __fmaf_rn(-mb0, s0, __fmaf_rn(db1, a1, -mb1 * s1)));
     } else if constexpr (DT == DT_Q6_K) {
         const int t = c & 7, sbl = cl >> 3;
@@ -323,12 +340,11 @@ __host__ __device__ inline size_t gemv_smem_total(int nc, int k, int vpc, int cr
     return gemv_x_bytes(nc, k, vpc, cr) + (size_t)pc.nstage * pc.sb + 2 * GEMV_MAX_STAGES * 8;
 }
 
-template <int DT, int NC, int R, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
+template <int DT, int NC, int R, int EPI, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(GemvArgs a) {
     constexpr int VPC = Fmt<DT>::VPC;
     constexpr int CR = Fmt<DT>::CR;
-    constexpr int TR = GEMV_CWARPS * R;
-    static_assert(TR <= 32, "one producer lane per tile row");
+    constexpr int TR = CW * R;
     const PipeCfg &pc = a.pc;
     const int K = a.w.k;
     const int C = K / VPC;
@@ -338,14 +354,14 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
     uint8_t *stages = cmolcu_smem + gemv_x_bytes(NC, K, VPC, CR);
     uint64_t *bar = reinterpret_cast<uint64_t *>(stages + (size_t)pc.nstage * pc.sb);
     uint64_t *full = bar, *empty = bar + GEMV_MAX_STAGES;
-    __shared__ float red[GEMV_CWARPS][NC];
+    __shared__ float red[CW][NC];
     __shared__ float inv_rms[NC];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     if (tid == 0) {
         for (int s = 0; s < pc.nstage; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], GEMV_CWARPS);
+            mbar_init(&empty[s], CW);
         }
         fence_mbar_init();
     }
@@ -358,7 +374,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
     const int ntile = (row_end - row_begin + TR - 1) / TR;
     const int nseq = ntile * a.w.nkc;
 
-    if (warp == GEMV_CWARPS) {
+    if (warp == CW) {
         // ---------------- producer warp ----------------
         // one bulk copy per plane and stage: rows r0..r0+nrow of K-chunk j
         // are contiguous in the K-chunk-major layout (qweight.cuh)
@@ -394,7 +410,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
             float ss[NC];
 #pragma unroll
             for (int c = 0; c < NC; c++) ss[c] = 0.f;
-            for (int i = tid; i < K; i += GEMV_CWARPS * 32) {
+            for (int i = tid; i < K; i += CW * 32) {
 #pragma unroll
                 for (int c = 0; c < NC; c++) {
                     float v = c < a.ncol ? a.x[(long long)c * a.x_ld + (long long)i * a.x_inc] : 0.f;
@@ -406,17 +422,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
                 float v = warp_sum(ss[c]);
                 if (lane == 0) red[warp][c] = v;
             }
-            named_bar_sync(1, GEMV_CWARPS * 32);
+            named_bar_sync(1, CW * 32);
             if (tid < NC) {
                 float t = 0.f;
-                for (int w = 0; w < GEMV_CWARPS; w++) t += red[w][tid];
+                for (int w = 0; w < CW; w++) t += red[w][tid];
                 inv_rms[tid] = 1.0f / sqrtf(t / (float)K + a.eps);
             }
-            named_bar_sync(1, GEMV_CWARPS * 32);
+            named_bar_sync(1, CW * 32);
         }
         // pass 2: one thread per (column, chunk, run): normalise, scale by
         // 2^85, store interleaved, and store the run sum (2^-64 domain)
-        for (int j = tid; j < NC * C * CR; j += GEMV_CWARPS * 32) {
+        for (int j = tid; j < NC * C * CR; j += CW * 32) {
             const int col = j / (C * CR), rem = j % (C * CR), c = rem / CR, p = rem % CR;
             int q0, q1;
             chunk_runs<DT>(c, q0, q1);
@@ -438,7 +454,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
             for (int i = 0; i < 4; i++) dst[i * 32] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             RS[(size_t)col * CP * CR + (size_t)(c >> 5) * CR * 32 + p * 32 + (c & 31)] = t * __int_as_float(1);
         }
-        named_bar_sync(1, GEMV_CWARPS * 32);
+        named_bar_sync(1, CW * 32);
     }
 
     int seq = 0;
