@@ -74,6 +74,16 @@ int cmolcu_gemv(const cmolcu_weight_t *w,
                 const float *norm_w, float eps,
                 float *y, long long y_ld, int y_inc, void *stream);
 
+/* ---- batched matmul on the tensor cores ------------------------------------
+ * y(c, r) = sum_k deq(W[r, k]) * xn(c, k) for c < n <= 256 columns, device
+ * buffers x [n][k] and y [n][rows], xn as in cmolcu_gemv.  Weights are
+ * dequantised to f16 and activations rounded to f16, products accumulate in
+ * f32 (tcgen05): results differ from cmolcu_gemv by about 2^-11 relative
+ * per term.  Q4_K, Q8_0, Q4_0 and Q5_0 only; k a multiple of 64.  Replaces
+ * the n > 1 use of src/quant.c:334-566 (which re-dequantises per column). */
+int cmolcu_matmul_batched(const cmolcu_weight_t *w, const float *x, int n, const float *norm_w, float eps,
+                          float *y, void *stream);
+
 /* Microbenchmark: `iters` back-to-back GEMVs (rotating over the nw weights,
  * all of one shape, n = 1 or 2 columns, x [n][k], y [n][rows] on the
  * device), captured once in a CUDA graph with programmatic dependent launch

@@ -66,6 +66,7 @@ def _declare(L):
     sig("cmolcu_gemv", C.c_int, [_vp, _vp, C.c_longlong, C.c_int, C.c_int, _vp, C.c_float,
                                  _vp, C.c_longlong, C.c_int, _vp])
     sig("cmolcu_matmul", None, [_fp, _vp, _fp, C.c_int, C.c_int, C.c_int, C.c_int])
+    sig("cmolcu_matmul_batched", C.c_int, [_vp, _vp, C.c_int, _vp, C.c_float, _vp, _vp])
     sig("cmolcu_fault_status", C.c_int, [C.c_int, C.POINTER(C.c_uint), C.c_int])
     sig("cmolcu_gemv_bench", C.c_int, [C.POINTER(_vp), C.c_int, _vp, C.c_int, _vp, C.c_int, C.c_int,
                                        C.POINTER(C.c_float)])
@@ -115,6 +116,12 @@ class Weight:
         check(lib().cmolcu_gemv(self.h, x.data_ptr(), x_ld, x_inc, n,
                                 norm_w.data_ptr() if norm_w is not None else None, eps,
                                 y.data_ptr(), y_ld, y_inc, stream), "cmolcu_gemv")
+
+    def matmul_batched(self, x, y, n: int, norm_w=None, eps: float = 1e-5, stream=None):
+        """y[n][rows] = W . xn on the tensor cores; x [n][k] (torch, device); see cmolcu_matmul_batched."""
+        check(lib().cmolcu_matmul_batched(self.h, x.data_ptr(), n,
+                                          norm_w.data_ptr() if norm_w is not None else None, eps,
+                                          y.data_ptr(), stream), "cmolcu_matmul_batched")
 
 
 def gemv_bench(weights, x, y, n: int, iters: int = 64, reps: int = 5) -> float:

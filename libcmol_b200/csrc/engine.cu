@@ -11,6 +11,7 @@
 
 #include "attention.cuh"
 #include "decode_step.cuh"
+#include "gemm_tc.cuh"
 #include "gemv_launch.cuh"
 #include "step_kernels.cuh"
 
@@ -68,6 +69,10 @@ struct Engine::Impl {
     unsigned int *ds_sync = nullptr;
     DsPlan        ds_plan[3];
     bool          ds_ok[3] = {false, false, false};
+    // tensor-core matmul for steps of >= tc_min_cols columns (gemm_tc.cuh)
+    TcScratch     tc = {};
+    bool          tc_ok = false;
+    int           tc_min_cols = 8;
     // CMOLCU_DS_TRACE=1: per-phase timing of CTA 0, summed over steps, printed at exit
     unsigned long long *ds_trace = nullptr;
     std::vector<unsigned long long> ds_trace_host;
@@ -243,6 +248,42 @@ static void build_step_kernel(Engine *e, Engine::Impl *d, EngineBuilder &b) {
     }
 }
 
+// Scratch of the tensor-core matmul, sized for the largest weight at
+// max_batch columns.  Steps of at least tc_min_cols columns use it for every
+// weight in a format it handles (Q4_K, Q8_0, Q4_0, Q5_0); the rest, and
+// smaller steps, use the exact f32 GEMV.  CMOLCU_TC_MIN_COLS overrides the
+// threshold (1 forces the tensor cores for every step).
+static void build_tensor_core_path(Engine *e, Engine::Impl *d, EngineBuilder &b) {
+    const EngineOptions &o = e->options();
+    const char *env = getenv("CMOLCU_TC_MIN_COLS");
+    if (env && atoi(env) > 0) d->tc_min_cols = atoi(env);
+    if (o.max_batch < d->tc_min_cols) return;
+    size_t xs = 0, part = 0;
+    int rbs = 0;
+    auto need = [&](const DevWeight &w) {
+        if (!w.base || !tc_supported(w.q.dtype)) return;
+        size_t a = 0, p = 0;
+        int r = 0;
+        tc_scratch_need(w.q.rows, w.q.k, o.max_batch, &a, &p, &r);
+        xs = std::max(xs, a);
+        part = std::max(part, p);
+        rbs = std::max(rbs, r);
+    };
+    for (const Layer &ly : d->layers) {
+        need(ly.qkv); need(ly.q); need(ly.k); need(ly.v);
+        need(ly.wo); need(ly.gu); need(ly.down);
+    }
+    need(d->head.base ? d->head : d->embd);
+    if (!xs) return;
+    d->tc.xs = b.dalloc<uint16_t>(xs);
+    d->tc.part = b.dalloc<float>(std::max<size_t>(part, 1));
+    d->tc.part_floats = part;
+    d->tc.counters = b.dalloc<int>((size_t)rbs);
+    d->tc.max_row_blocks = rbs;
+    d->tc_ok = d->tc.xs && d->tc.part && d->tc.counters;
+    if (!d->tc_ok) cudaGetLastError();
+}
+
 Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, int *err, char *msg, int msg_len) {
     const HParams &hp = m.hp;
     *err = -4;  // CMOL_ERR_UNSUPPORTED
@@ -412,6 +453,7 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
         d->n_pages = n;
     }
     build_step_kernel(e, d, b);
+    build_tensor_core_path(e, d, b);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(-1);
     *err = 0;
     return e;
@@ -475,6 +517,18 @@ int Engine::set_sampler(int slot, const SamplerParams &p) {
     return 0;
 }
 
+// One weight product of a step: the tensor cores when the step is wide
+// enough and the format has a tensor-core path, else the f32 GEMV.
+static cudaError_t step_matmul(Engine::Impl *d, const GemvArgs &a, int ncol, int epi, cudaStream_t st, bool pdl,
+                               int &launches) {
+    if (d->tc_ok && ncol >= d->tc_min_cols && tc_supported(a.w.dtype) && a.w.k % TC_KB == 0 && a.w.kc % TC_KB == 0) {
+        launches += 2;
+        return tc_matmul(a, ncol, epi, d->tc, st, pdl);
+    }
+    launches += (ncol + 1) / 2;
+    return gemv_launch_cols(a, ncol, epi, st, pdl);
+}
+
 // Records the kernels of one step for `ncol` columns on the engine stream.
 static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol, int max_pages, int &launches,
                                bool gemv_only = false) {
@@ -485,7 +539,6 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
     const bool pdl = true;
     cudaError_t e;
     launches = 0;
-    auto gemv_ncalls = [&](int n) { return (n + 1) / 2; };
 
     StepBeginArgs sb = {};
     sb.meta = d->meta;
@@ -561,14 +614,12 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             a.norm_w = ly.attn_norm;
             if (qkn) {   // raw projections; norm + RoPE + KV append in the next kernel
                 a.y = d->qkvbuf + row_base; a.y_ld = D + 2 * KVD;
-                launches += gemv_ncalls(ncol);
-                return gemv_launch_cols(a, ncol, EPI_STORE, st, pdl);
+                return step_matmul(d, a, ncol, EPI_STORE, st, pdl, launches);
             }
             a.y = d->qbuf; a.y_ld = D;
             a.qkv = q;
             a.qkv.row_base = row_base;
-            launches += gemv_ncalls(ncol);
-            return gemv_launch_cols(a, ncol, EPI_QKV, st, pdl);
+            return step_matmul(d, a, ncol, EPI_QKV, st, pdl, launches);
         };
         if (ly.fused_qkv) {
             if ((e = qkv_part(ly.qkv, 0)) != cudaSuccess) return e;
@@ -608,8 +659,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             a.w = ly.wo.q;
             a.x = d->attn; a.x_ld = D;
             a.y = d->x; a.y_ld = D;
-            if ((e = gemv_launch_cols(a, ncol, EPI_RESID, st, pdl)) != cudaSuccess) return e;
-            launches += gemv_ncalls(ncol);
+            if ((e = step_matmul(d, a, ncol, EPI_RESID, st, pdl, launches)) != cudaSuccess) return e;
         }
         // --- FFN: norm + gate/up + SwiGLU, then down + residual --------------
         {
@@ -618,16 +668,14 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             a.x = d->x; a.x_ld = D;
             a.norm_w = ly.ffn_norm;
             a.y = d->h; a.y_ld = F;
-            if ((e = gemv_launch_cols(a, ncol, EPI_SWIGLU, st, pdl)) != cudaSuccess) return e;
-            launches += gemv_ncalls(ncol);
+            if ((e = step_matmul(d, a, ncol, EPI_SWIGLU, st, pdl, launches)) != cudaSuccess) return e;
         }
         {
             GemvArgs a = g;
             a.w = ly.down.q;
             a.x = d->h; a.x_ld = F;
             a.y = d->x; a.y_ld = D;
-            if ((e = gemv_launch_cols(a, ncol, EPI_RESID, st, pdl)) != cudaSuccess) return e;
-            launches += gemv_ncalls(ncol);
+            if ((e = step_matmul(d, a, ncol, EPI_RESID, st, pdl, launches)) != cudaSuccess) return e;
         }
     }
     // --- final norm + LM head, sampler ----------------------------------------
@@ -637,8 +685,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         a.x = d->x; a.x_ld = D;
         a.norm_w = d->out_norm;
         a.y = d->logits; a.y_ld = V;
-        if ((e = gemv_launch_cols(a, ncol, EPI_STORE, st, pdl)) != cudaSuccess) return e;
-        launches += gemv_ncalls(ncol);
+        if ((e = step_matmul(d, a, ncol, EPI_STORE, st, pdl, launches)) != cudaSuccess) return e;
     }
     if (gemv_only) return cudaSuccess;
     SampleArgs sa = {};

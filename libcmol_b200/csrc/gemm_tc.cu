@@ -1,0 +1,472 @@
+// gemm_tc.cu — batched dequant matmul on tcgen05 tensor cores (see gemm_tc.cuh).
+#include "gemm_tc.cuh"
+#include "gemv_launch.cuh"
+
+#include <algorithm>
+
+#define TC_DQW 8                          // dequantising warps (2..9)
+#define TC_THREADS ((2 + TC_DQW) * 32)    // + producer warp 0, MMA warp 1
+#define TC_DQT (TC_DQW * 32)
+
+bool tc_supported(int dt) { return dt == DT_Q4_K || dt == DT_Q8_0 || dt == DT_Q4_0 || dt == DT_Q5_0; }
+
+// ---------------------------------------------------------------------------
+// tcgen05 / proxy helpers (inline PTX, sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// K-major operand with the 128-byte swizzle: rows of 128 bytes (64 f16),
+// 8-row groups 1024 bytes apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);      // start address
+    d |= (uint64_t)1 << 16;                        // leading byte offset (16 B; unused for this layout)
+    d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset
+    d |= (uint64_t)1 << 46;                        // version
+    d |= (uint64_t)2 << 61;                        // 128-byte swizzle
+    return d;
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// ---------------------------------------------------------------------------
+// Activation image: one CTA per column (columns >= ncol are zero).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_tc_xprep(const float *x, long long x_ld, int K, int ncol, int npad,
+                                                  const float *norm_w, float eps, uint16_t *xs) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float red[8];
+    __shared__ float s_ir;
+    const bool live = n < ncol;
+    const float *xc = x + (long long)n * x_ld;
+    float ir = 1.f;
+    if (live && norm_w) {
+        // the RMS of src/model.c:90-97, in the GEMV's summation order
+        float ss = 0.f;
+        for (int i = tid; i < K; i += 256) {
+            const float v = xc[i];
+            ss = __fmaf_rn(v, v, ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.f;
+            for (int w = 0; w < 8; w++) t += red[w];
+            s_ir = 1.0f / sqrtf(t / (float)K + eps);
+        }
+        __syncthreads();
+        ir = s_ir;
+    }
+    for (int c = tid; c < K / 8; c += 256) {
+        const int k0 = c * 8, kb = k0 >> 6, ch = (k0 & 63) >> 3;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float t = live ? xc[k0 + i] : 0.f;
+            if (live && norm_w) t = __fmul_rn(norm_w[k0 + i], __fmul_rn(t, ir));
+            v[i] = t;
+        }
+        uint4 o = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+        uint4 *dst = reinterpret_cast<uint4 *>(xs + ((size_t)kb * npad + n) * 64) + (ch ^ (n & 7));
+        *dst = o;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// The matmul
+// ---------------------------------------------------------------------------
+struct TcParams {
+    GemvArgs        g;                 // weight, y, epilogue fields
+    int             epi, ncol, npad;
+    const uint16_t *xs;
+    int             ksplit, chunks_per_split;
+    float          *part;
+    int            *counters;
+    int             q_off[4];          // plane offsets in the quantised stage (TC_M rows of a full K-chunk each)
+    uint32_t        tmem_cols;
+};
+
+// 16 dequantised values of row r, values [v, v + 16) of the K-chunk held in
+// the quantised stage (GGUF block arithmetic of src/quant.c:152-194).
+template <int DT>
+__device__ __forceinline__ void tc_dequant16(const uint8_t *q, const int *q_off, const int *st, int r, int v,
+                                             float out[16]) {
+    const uint8_t *P0 = q + q_off[0] + r * st[0];
+    const uint8_t *P1 = q + q_off[1] + r * st[1];
+    if constexpr (DT == DT_Q4_K) {
+        const int s = v >> 8, o = v & 255, pj = o >> 6, half = (o >> 5) & 1, sub = (o >> 4) & 1;
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + s * 128 + 32 * pj + 16 * sub);
+        const uint4 h = *reinterpret_cast<const uint4 *>(P1 + s * 16);
+        const float d = h2f((uint16_t)(h.x & 0xFFFF)), dmin = h2f((uint16_t)(h.x >> 16));
+        float sc0, sc1, mn0, mn1;
+        q4k_pair(h.y, h.z, h.w, pj, sc0, sc1, mn0, mn1);
+        const float a = d * (half ? sc1 : sc0), m = dmin * (half ? mn1 : mn0);
+        const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const uint32_t b = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+            const float nib = (float)(half ? (b >> 4) : (b & 15u));
+            out[i] = __fmaf_rn(a, nib, -m);
+        }
+    } else if constexpr (DT == DT_Q8_0) {
+        const int b = v >> 5, hh = (v >> 4) & 1;
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 32 + 16 * hh);
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
+        const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
+#pragma unroll
+        for (int i = 0; i < 16; i++) out[i] = d * (float)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFFu);
+    } else {   // Q4_0, Q5_0
+        const int b = v >> 5, hh = (v >> 4) & 1;
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 16);
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
+        uint32_t qh = 0;
+        if constexpr (DT == DT_Q5_0) qh = *reinterpret_cast<const uint32_t *>(q + q_off[2] + r * st[2] + b * 4);
+        const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+            int nib = (int)(hh ? (byte >> 4) : (byte & 15u));
+            if constexpr (DT == DT_Q5_0) nib = (nib | (int)(((qh >> (16 * hh + i)) & 1u) << 4)) - 16;
+            else nib -= 8;
+            out[i] = d * (float)nib;
+        }
+    }
+}
+
+// Epilogue of one value (STORE, RESID) or of a row pair (SWIGLU, QKV; the
+// even row's thread writes).
+__device__ __forceinline__ void tc_epilogue(const TcParams &p, int row, int col, float v, float partner) {
+    const GemvArgs &g = p.g;
+    if (row >= g.w.rows || col >= p.ncol) return;
+    switch (p.epi) {
+    case EPI_STORE:
+        g.y[(long long)col * g.y_ld + row] = v;
+        break;
+    case EPI_RESID: {
+        float *y = g.y + (long long)col * g.y_ld + row;
+        *y = __ldcg(y) + v;
+        break;
+    }
+    case EPI_SWIGLU:
+        if (!(row & 1) && row + 1 < g.w.rows) epi_swiglu_pair(g, row, col, v, partner);
+        break;
+    default:
+        if (!(row & 1) && row + 1 < g.w.rows) epi_qkv_pair(g, row, col, v, partner);
+        break;
+    }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant__ TcParams p) {
+    const QWeight &w = p.g.w;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rb = blockIdx.x, ks = blockIdx.y;
+    const int m0 = rb * TC_M;
+    const int npad = p.npad;
+    const int j0 = ks * p.chunks_per_split, j1 = min(w.nkc, j0 + p.chunks_per_split);
+
+    // shared memory: A tiles, B tiles, quantised stage (all 1024-aligned), then barriers
+    uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
+    uint8_t *A = base;                                        // 2 x 16 KB
+    uint8_t *B = A + 2 * TC_M * 128;                          // 2 x npad * 128
+    uint8_t *Q = B + 2 * (size_t)npad * 128;                  // quantised K-chunk
+    const int qbytes = p.q_off[3] + TC_M * (w.nplanes > 3 ? w.cs[3] : 0);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(Q + ((qbytes + 127) & ~127));
+    uint64_t *qfull = bars, *qempty = bars + 1, *afull = bars + 2, *aempty = bars + 4, *bfull = bars + 6,
+             *bempty = bars + 8, *accfull = bars + 10;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_last;
+
+    if (tid == 0) {
+        mbar_init(qfull, 1);
+        mbar_init(qempty, TC_DQW);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&afull[i], TC_DQW);
+            mbar_init(&aempty[i], 1);
+            mbar_init(&bfull[i], 1);
+            mbar_init(&bempty[i], 1);
+        }
+        mbar_init(accfull, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    pdl_launch_dependents();
+
+    // k-blocks of this CTA: every K-chunk holds a whole number of them
+    int nkb = 0;
+    for (int j = j0; j < j1; j++) nkb += qw_chunk_values(w, j) / TC_KB;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const int nrow = min(TC_M, w.prow - m0);
+            int bn = 0;
+            for (int j = j0; j < j1; j++) {
+                const int qi = j - j0;
+                if (qi > 0 && !mbar_wait(qempty, (qi - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) break;
+                int bytes = 0;
+                for (int pl = 0; pl < w.nplanes; pl++) bytes += nrow * qw_stride(w, pl, j);
+                mbar_arrive_expect_tx(qfull, (uint32_t)bytes);
+                for (int pl = 0; pl < w.nplanes; pl++)
+                    bulk_g2s(Q + p.q_off[pl], qw_row(w, pl, j, m0), (uint32_t)(nrow * qw_stride(w, pl, j)), qfull);
+                if (qi == 0) pdl_wait();   // the activation image comes from the previous kernel
+                const int kbs = qw_chunk_values(w, j) / TC_KB;
+                const int g0 = (j * w.kc) / TC_KB;
+                bool ok = true;
+                for (int i = 0; i < kbs; i++, bn++) {
+                    const int slot = bn & 1, use = bn >> 1;
+                    if (use > 0 && !mbar_wait(&bempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&bfull[slot], (uint32_t)(npad * 128));
+                    bulk_g2s(B + (size_t)slot * npad * 128, p.xs + (size_t)(g0 + i) * npad * 64, (uint32_t)(npad * 128),
+                             &bfull[slot]);
+                }
+                if (!ok) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(npad >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+            for (int i = 0; i < nkb; i++) {
+                const int slot = i & 1, use = i >> 1;
+                mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
+                mbar_wait(&bfull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(A + slot * TC_M * 128), b_addr = smem_u32(B + (size_t)slot * npad * 128);
+#pragma unroll
+                for (int k = 0; k < TC_KB / 16; k++)
+                    tc_mma(tmem, tc_desc(a_addr + 32 * k), tc_desc(b_addr + 32 * k), idesc, (i | k) != 0);
+                tc_commit(&aempty[slot]);
+                tc_commit(&bempty[slot]);
+            }
+            tc_commit(accfull);
+        }
+    } else {
+        // ---------------- dequantise ----------------
+        const int dt = tid - 64;
+        int i = 0;
+        for (int j = j0; j < j1; j++) {
+            const int qi = j - j0;
+            mbar_wait(qfull, qi & 1, p.g.fault, FAULT_GEMV_FULL);
+            int st[4];
+#pragma unroll
+            for (int pl = 0; pl < 4; pl++) st[pl] = qw_stride(w, pl, j);
+            const int kbs = qw_chunk_values(w, j) / TC_KB;
+            for (int ib = 0; ib < kbs; ib++, i++) {
+                const int slot = i & 1, use = i >> 1;
+                if (use > 0) mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY);
+                uint8_t *tile = A + slot * TC_M * 128;
+                // task = (row r, 16-value run q): 128 rows x 4 runs
+#pragma unroll
+                for (int t = 0; t < (TC_M * 4) / TC_DQT; t++) {
+                    const int task = dt + TC_DQT * t, r = task >> 2, q = task & 3;
+                    float v[16];
+                    tc_dequant16<DT>(Q, p.q_off, st, r, ib * TC_KB + 16 * q, v);
+                    const uint4 lo = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
+                                                pack_h2(v[6], v[7]));
+                    const uint4 hi = make_uint4(pack_h2(v[8], v[9]), pack_h2(v[10], v[11]), pack_h2(v[12], v[13]),
+                                                pack_h2(v[14], v[15]));
+                    uint4 *row = reinterpret_cast<uint4 *>(tile + r * 128);
+                    row[(2 * q) ^ (r & 7)] = lo;
+                    row[(2 * q + 1) ^ (r & 7)] = hi;
+                }
+                fence_proxy_async_smem();   // the tensor core reads the tile through the async proxy
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[slot]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(qempty);
+        }
+        // ---------------- epilogue: tensor memory -> registers ----------------
+        if (warp < 6) {
+            const int quarter = warp & 3;                 // the TMEM lanes this warp may read
+            const int row = m0 + 32 * quarter + lane;
+            mbar_wait(accfull, 0, p.g.fault, FAULT_GEMV_FULL);
+            tc_fence_after();
+            if (p.ksplit == 1) pdl_wait();
+            for (int c0 = 0; c0 < npad; c0 += 16) {
+                float v[16];
+                tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+                if (p.ksplit == 1) {
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 1);
+                        tc_epilogue(p, row, c0 + e, v[e], partner);
+                    }
+                } else {
+                    float *pp = p.part + ((size_t)(rb * p.ksplit + ks) * npad + c0) * TC_M + (row - m0);
+#pragma unroll
+                    for (int e = 0; e < 16; e++) pp[(size_t)e * TC_M] = v[e];
+                }
+            }
+        }
+    }
+
+    // ---------------- split-K: the last CTA of the row block adds the partials ----------------
+    tc_fence_before();
+    __syncthreads();
+    if (p.ksplit > 1) {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(&p.counters[rb], 1) == p.ksplit - 1;
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            pdl_wait();
+            // thread = (row pair, column): the even row's thread applies pair epilogues
+            for (int idx = tid; idx < (TC_M / 2) * npad; idx += TC_THREADS) {
+                const int rp = idx % (TC_M / 2), col = idx / (TC_M / 2);
+                const int r = 2 * rp;
+                float v0 = 0.f, v1 = 0.f;
+                for (int s = 0; s < p.ksplit; s++) {
+                    const float *pp = p.part + ((size_t)(rb * p.ksplit + s) * npad + col) * TC_M + r;
+                    v0 += __ldcg(pp);
+                    v1 += __ldcg(pp + 1);
+                }
+                const int row = m0 + r;
+                if (p.epi == EPI_STORE || p.epi == EPI_RESID) {
+                    tc_epilogue(p, row, col, v0, v1);
+                    tc_epilogue(p, row + 1, col, v1, v0);
+                } else {
+                    tc_epilogue(p, row, col, v0, v1);
+                }
+            }
+            if (tid == 0) p.counters[rb] = 0;
+        }
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static int tc_npad(int ncol) { return std::max(16, (ncol + 15) / 16 * 16); }
+
+static void tc_split(int rows, int nkc, int &rblocks, int &ksplit, int &cps) {
+    const int sms = device_sm_count();
+    rblocks = (rows + TC_M - 1) / TC_M;
+    ksplit = std::max(1, std::min(nkc, (sms + rblocks - 1) / rblocks));
+    cps = (nkc + ksplit - 1) / ksplit;
+    ksplit = (nkc + cps - 1) / cps;
+}
+
+void tc_scratch_need(int rows, int k, int ncol, size_t *xs_halves, size_t *part_floats, int *row_blocks) {
+    const int npad = tc_npad(ncol);
+    *xs_halves = (size_t)k * npad;
+    // the K-chunk count is at most k / 512 + 1 for the supported formats
+    int rb, ks, cps;
+    tc_split(rows, k / 512 + 1, rb, ks, cps);
+    *part_floats = ks > 1 ? (size_t)rb * ks * npad * TC_M : 0;
+    *row_blocks = rb;
+}
+
+typedef void (*tc_kernel_t)(TcParams);
+
+static tc_kernel_t tc_pick(int dt) {
+    switch (dt) {
+    case DT_Q4_K: return k_tc_gemm<DT_Q4_K>;
+    case DT_Q8_0: return k_tc_gemm<DT_Q8_0>;
+    case DT_Q4_0: return k_tc_gemm<DT_Q4_0>;
+    case DT_Q5_0: return k_tc_gemm<DT_Q5_0>;
+    default: return nullptr;
+    }
+}
+
+cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, cudaStream_t st, bool pdl) {
+    const QWeight &w = a.w;
+    tc_kernel_t k = tc_pick(w.dtype);
+    if (!k || ncol < 1 || ncol > TC_MAX_N || w.k % TC_KB || w.kc % TC_KB || a.x_inc != 1 || a.y_inc != 1)
+        return cudaErrorInvalidValue;
+    const int npad = tc_npad(ncol);
+    int rb, ks, cps;
+    tc_split(w.rows, w.nkc, rb, ks, cps);
+    if ((size_t)w.k * npad > ((size_t)1 << 40) || !s.xs || rb > s.max_row_blocks ||
+        (ks > 1 && (size_t)rb * ks * npad * TC_M > s.part_floats))
+        return cudaErrorInvalidValue;
+    TcParams p = {};
+    p.g = a;
+    p.g.ncol = ncol;
+    p.epi = epi;
+    p.ncol = ncol;
+    p.npad = npad;
+    p.xs = s.xs;
+    p.ksplit = ks;
+    p.chunks_per_split = cps;
+    p.part = s.part;
+    p.counters = s.counters;
+    int off = 0;
+    for (int pl = 0; pl < 4; pl++) {
+        p.q_off[pl] = off;
+        off += pl < w.nplanes ? TC_M * w.cs[pl] : 0;
+    }
+    p.tmem_cols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
+    const size_t smem = 1024 + 2 * TC_M * 128 + 2 * (size_t)npad * 128 + (((size_t)off + 127) & ~(size_t)127) + 16 * 8;
+    static size_t attr_done[64][4];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int di = w.dtype == DT_Q4_K ? 0 : w.dtype == DT_Q8_0 ? 1 : w.dtype == DT_Q4_0 ? 2 : 3;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_done[dev][di]) {
+        // the dynamic limit is the opt-in maximum minus the kernel's static shared memory
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaFuncAttributes fa = {};
+        cudaError_t e = cudaFuncGetAttributes(&fa, k);
+        if (e != cudaSuccess) return e;
+        const size_t lim = (size_t)optin - fa.sharedSizeBytes;
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lim);
+        if (e != cudaSuccess) return e;
+        attr_done[dev][di] = lim;
+    }
+    if (smem > attr_done[dev][di]) return cudaErrorInvalidConfiguration;
+    cudaError_t e = launch_k(k_tc_xprep, dim3(npad), dim3(256), 0, st, pdl, a.x, a.x_ld, w.k, ncol, npad, a.norm_w,
+                             a.eps, s.xs);
+    if (e != cudaSuccess) return e;
+    return launch_k(k, dim3(rb, ks), dim3(TC_THREADS), smem, st, pdl, p);
+}

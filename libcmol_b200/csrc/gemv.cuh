@@ -259,6 +259,49 @@ template <int DT> __device__ __forceinline__ float final_scale() {
     else return kQScaleInv;
 }
 
+// Rows 2i (gate) and 2i+1 (up) -> h[i] = silu(g) * u   (src/model.c:117-123)
+__device__ __forceinline__ void epi_swiglu_pair(const GemvArgs &a, int row, int col, float g, float u) {
+    float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    a.y[(long long)col * a.y_ld + (long long)(row / 2) * a.y_inc] = h;
+}
+
+// Fused Q/K/V rows (lrow, lrow+1) of column col (local row numbering; the
+// global row adds qkv.row_base): RoPE on q and k pairs, q to y, k and v into
+// the column's KV page at its position.
+__device__ __forceinline__ void epi_qkv_pair(const GemvArgs &a, int lrow, int col, float v0, float v1) {
+    const EpiQKV &e = a.qkv;
+    const int row = e.row_base + lrow;
+    const int pos = e.pos[col];
+    if (pos < 0) return;
+    const int D = e.d_model, KVD = e.kv_dim, hd = e.d_head;
+    const bool is_v = row >= D + KVD;
+    if (e.rope && !is_v) {
+        // NORM-style pair rotation, src/model.c:137-166
+        int i = (row % hd) >> 1;
+        float2 cs = e.rope_cs[(long long)pos * (hd / 2) + i];
+        float n0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+        float n1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+        v0 = n0; v1 = n1;
+    }
+    if (row < D) {
+        float *q = a.y + (long long)col * a.y_ld;
+        q[row] = v0; q[row + 1] = v1;
+        return;
+    }
+    const int kvr = is_v ? row - D - KVD : row - D;
+    const int head = kvr / hd, dim = kvr % hd;
+    const int srow = e.slot ? e.slot[col] : col;
+    const int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
+    if (pg < 0 || pg >= e.n_pages) {   // never write outside the pool
+        if (a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
+        return;
+    }
+    const int t = pos % e.page_tokens;
+    float *base = e.kv_pages + (long long)pg * e.page_floats +
+                  ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd + dim;
+    base[0] = v0; base[1] = v1;
+}
+
 // Epilogue; vals[r*NC+col] hold the totals of rows row0..row0+R-1.
 template <int NC, int R, int EPI>
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const float *vals, int lane) {
@@ -275,52 +318,17 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const
             }
         }
     } else if constexpr (EPI == EPI_SWIGLU) {
-        // rows 2i (gate) and 2i+1 (up) -> h[i] = silu(g)*u   (src/model.c:117-123)
         if (lane < (R / 2) * NC) {
             int p = lane / NC, col = lane % NC;
             int row = row0 + 2 * p;
-            if (row + 1 < rows && col < a.ncol) {
-                float g = vals[(2 * p) * NC + col], u = vals[(2 * p + 1) * NC + col];
-                float h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-                a.y[(long long)col * a.y_ld + (long long)(row / 2) * a.y_inc] = h;
-            }
+            if (row + 1 < rows && col < a.ncol)
+                epi_swiglu_pair(a, row, col, vals[(2 * p) * NC + col], vals[(2 * p + 1) * NC + col]);
         }
     } else {  // EPI_QKV
         if (lane < (R / 2) * NC) {
-            const EpiQKV &e = a.qkv;
             int p = lane / NC, col = lane % NC;
-            int row = e.row_base + row0 + 2 * p;
-            int pos = (col < a.ncol) ? e.pos[col] : -1;
-            if (row0 + 2 * p + 1 < rows && pos >= 0) {
-                float v0 = vals[(2 * p) * NC + col], v1 = vals[(2 * p + 1) * NC + col];
-                int D = e.d_model, KVD = e.kv_dim, hd = e.d_head;
-                bool is_v = row >= D + KVD;
-                if (e.rope && !is_v) {
-                    // NORM-style pair rotation, src/model.c:137-166
-                    int i = (row % hd) >> 1;
-                    float2 cs = e.rope_cs[(long long)pos * (hd / 2) + i];
-                    float n0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-                    float n1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
-                    v0 = n0; v1 = n1;
-                }
-                if (row < D) {
-                    float *q = a.y + (long long)col * a.y_ld;
-                    q[row] = v0; q[row + 1] = v1;
-                } else {
-                    int kvr = is_v ? row - D - KVD : row - D;
-                    int head = kvr / hd, dim = kvr % hd;
-                    int srow = e.slot ? e.slot[col] : col;
-                    int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
-                    if (pg < 0 || pg >= e.n_pages) {   // never write outside the pool
-                        if (a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
-                        return;
-                    }
-                    int t = pos % e.page_tokens;
-                    float *base = e.kv_pages + (long long)pg * e.page_floats +
-                                  ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd + dim;
-                    base[0] = v0; base[1] = v1;
-                }
-            }
+            if (row0 + 2 * p + 1 < rows && col < a.ncol)
+                epi_qkv_pair(a, row0 + 2 * p, col, vals[(2 * p) * NC + col], vals[(2 * p + 1) * NC + col]);
         }
     }
 }

@@ -1,5 +1,6 @@
 // seam.cu — the C ABI of cmolcu.h (weights, GEMV, host matmul seam).
 #include "../../include/cmolcu.h"
+#include "gemm_tc.cuh"
 #include "gemv_launch.cuh"
 
 #include <stdarg.h>
@@ -172,6 +173,42 @@ extern "C" void cmolcu_matmul(float *out, const void *a, const float *b, int m, 
     cudaFree(db);
     cudaFree(dy);
     cmolcu_weight_free(w);
+}
+
+extern "C" int cmolcu_matmul_batched(const cmolcu_weight_t *w, const float *x, int n, const float *norm_w,
+                                     float eps, float *y, void *stream) {
+    if (!w || !x || !y || n < 1 || n > TC_MAX_N) { cmolcu_set_error("cmolcu_matmul_batched: bad arguments"); return -1; }
+    if (!tc_supported(w->w.dtype)) {
+        cmolcu_set_error("cmolcu_matmul_batched: dtype %d has no tensor-core path", w->w.dtype);
+        return -1;
+    }
+    CUDA_TRY(cudaSetDevice(w->device));
+    size_t xh = 0, pf = 0;
+    int rb = 0;
+    tc_scratch_need(w->w.rows, w->w.k, n, &xh, &pf, &rb);
+    TcScratch sc = {};
+    cudaError_t e = cudaMalloc(&sc.xs, xh * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&sc.part, std::max<size_t>(pf, 1) * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&sc.counters, (size_t)rb * 4);
+    if (e == cudaSuccess) e = cudaMemset(sc.counters, 0, (size_t)rb * 4);
+    sc.part_floats = pf;
+    sc.max_row_blocks = rb;
+    unsigned int *fw = cmolcu_fault_word(w->device);
+    if (e == cudaSuccess) {
+        GemvArgs a = {};
+        a.w = w->w;
+        a.x = x; a.x_ld = w->w.k; a.x_inc = 1;
+        a.norm_w = norm_w; a.eps = eps;
+        a.y = y; a.y_ld = w->w.rows; a.y_inc = 1;
+        a.fault = fw;
+        e = tc_matmul(a, n, EPI_STORE, sc, (cudaStream_t)stream, false);
+        if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    }
+    cudaFree(sc.xs);
+    cudaFree(sc.part);
+    cudaFree(sc.counters);
+    if (e != cudaSuccess) { cmolcu_set_error("cmolcu_matmul_batched: %s", cudaGetErrorString(e)); return -1; }
+    return 0;
 }
 
 // Back-to-back GEMVs over `nw` distinct weights (all the same shape), captured

@@ -79,6 +79,52 @@ def test_teacher_forced_logits(gpu, golden, paths, name):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", MODELS)
+def test_teacher_forced_logits_tensor_cores(gpu, golden, paths, name, monkeypatch):
+    """The tensor-core matmul forced on every step (CMOLCU_TC_MIN_COLS=1):
+    f16 weights and activations, f32 accumulation.  Same tolerance as the
+    engine's spec; formats without a tensor-core path (Q6_K) keep the GEMV."""
+    from libcmol_b200.model import Model
+    monkeypatch.setenv("CMOLCU_TC_MIN_COLS", "1")
+    with Model(paths[name], max_ctx=64, max_sessions=2, page_tokens=4) as m:
+        s = m.acquire()
+        toks = golden[f"{name}_tokens"]
+        worst, wcos = 0.0, 1.0
+        for i, t in enumerate(toks):
+            got = s.forward_logits(int(t))
+            ref = golden[f"{name}_logits"][i]
+            d = float(np.abs(got - ref).max())
+            c = _cos(got, ref)
+            worst, wcos = max(worst, d), min(wcos, c)
+            assert d <= ATOL and c >= COS, (i, d, c)
+        print(f"{name}: tensor-core logits max-abs {worst:.2e} cos {wcos:.7f}")
+        s.release()
+
+
+@pytest.mark.gpu
+def test_wide_batch_uses_tensor_cores(gpu, golden, paths):
+    """Eight sessions in one step take the tensor-core path (default
+    threshold); every session decodes to the requested length, and the
+    greedy streams agree with the reference up to f16 rounding (reported)."""
+    from libcmol_b200.model import GenParams, Model
+    name = "q4_k"
+    with Model(paths[name], max_ctx=64, max_sessions=8) as m:
+        ss = [m.acquire() for _ in range(8)]
+        prompt = golden[f"{name}_tokens"][:6]
+        p = GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=20)
+        outs = m.generate_batch(ss, [prompt] * 8, [p] * 8)
+        ref = golden[f"{name}_gen_greedy"].tolist()
+        assert all(len(o) == len(ref) for o in outs)
+        same = sum(o.tolist() == ref for o in outs)
+        print(f"wide batch: {same}/8 streams identical to the reference")
+        assert all(o[0] == ref[0] for o in outs)
+        st = m.stats(0)
+        assert st.kernel_launches_per_step > 0
+        for s in ss:
+            s.release()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", MODELS)
 @pytest.mark.parametrize("tag", ["greedy", "greedy_pen", "topp", "topk"])
 def test_generate_matches_reference(gpu, golden, paths, name, tag):
     from libcmol_b200.model import Model

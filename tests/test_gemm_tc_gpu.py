@@ -1,0 +1,77 @@
+"""Batched dequant matmul on the tensor cores (cmolcu_matmul_batched).
+
+The checker is the oracle's dequantisation of the identical GGUF blocks
+(restating src/quant.c:152-194) times the activations in float64.  The
+tensor-core path rounds the dequantised weights and the activations to f16
+(11-bit significands) and accumulates in f32, so each product carries a
+relative error of at most about 2 * 2^-11; the bound is
+
+    |gpu - exact| <= 2.5e-3 * sum_k |w_k x_k| + 1e-6.
+"""
+import numpy as np
+import pytest
+
+from libcmol_b200 import synth
+
+REL = 2.5e-3
+CASES = [
+    (synth.Q4_K, 256, 1024, 16),      # two row blocks, split K
+    (synth.Q4_K, 384, 2048, 40),      # ragged column count
+    (synth.Q8_0, 200, 960, 24),       # rows not a multiple of 128, a short last K-chunk
+    (synth.Q4_0, 128, 576, 7),        # one K-chunk
+    (synth.Q5_0, 512, 2048, 64),
+    (synth.Q8_0, 19200, 512, 16),     # > 148 row blocks: no K split, epilogue from tensor memory
+    (synth.Q4_K, 1024, 4096, 256),    # the widest column count
+]
+
+
+def _dequant(blob, rows, k, dtype):
+    from oracle.oracle import Oracle
+    return np.stack([Oracle.dequant(blob[r], k, dtype) for r in range(rows)]).astype(np.float64)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,rows,k,n", CASES,
+                         ids=[f"{synth.DTYPE_NAMES[c[0]]}-{c[1]}x{c[2]}-n{c[3]}" for c in CASES])
+@pytest.mark.parametrize("norm", [False, True], ids=["plain", "rmsnorm"])
+def test_batched_matches_exact(gpu, dtype, rows, k, n, norm):
+    import torch
+    from libcmol_b200 import Weight
+    rng = np.random.default_rng(rows + k + n)
+    wq = (rng.standard_normal((rows, k), dtype=np.float32) * 0.02).astype(np.float32)
+    blob = synth.quantize(wq, dtype)
+    x = rng.standard_normal((n, k), dtype=np.float32)
+    gains = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    W = Weight(blob, dtype, rows, k)
+    xd = torch.from_numpy(x).to(gpu)
+    yd = torch.full((n, rows), float("nan"), dtype=torch.float32, device=gpu)
+    gd = torch.from_numpy(gains).to(gpu) if norm else None
+    eps = 1e-5
+    W.matmul_batched(xd, yd, n, norm_w=gd, eps=eps)
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy().astype(np.float64)
+    xn = x.astype(np.float64)
+    if norm:
+        inv = 1.0 / np.sqrt((xn * xn).mean(axis=1, keepdims=True) + eps)
+        xn = xn * inv * gains.astype(np.float64)
+    Wd = _dequant(blob, rows, k, dtype)
+    want = xn @ Wd.T
+    bound = REL * (np.abs(xn) @ np.abs(Wd).T) + 1e-6
+    err = np.abs(got - want)
+    assert np.isfinite(got).all()
+    worst = np.unravel_index(np.argmax(err - bound), err.shape)
+    assert np.all(err <= bound), f"err {err[worst]} > bound {bound[worst]} at {worst}"
+    W.free()
+
+
+@pytest.mark.gpu
+def test_batched_rejects_unsupported(gpu):
+    import torch
+    from libcmol_b200 import CmolError, Weight
+    blob = synth.quantize(np.zeros((64, 256), np.float32), synth.Q6_K)
+    W = Weight(blob, synth.Q6_K, 64, 256)
+    x = torch.zeros(16, 256, device=gpu)
+    y = torch.zeros(16, 64, device=gpu)
+    with pytest.raises(CmolError, match="tensor-core"):
+        W.matmul_batched(x, y, 16)
+    W.free()
