@@ -6,7 +6,7 @@ random prompt, greedy decoding.  A "step" is one decode step: one token per
 session through all 32 layers, the LM head and the sampler.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c2|c5]
+                    [--workload c1|c2|c3|c4|c5]
 
 Multi-GPU runs are launched with torch.distributed.run, one process per GPU;
 sessions are independent (weights replicated, no collective on the data
@@ -46,7 +46,92 @@ WORKLOADS = {
                                       "distinct weight copies totalling > 2x L2"),
 }
 
+WORKLOADS["c3"] = dict(cfg=3, sessions=64, prompt=(16, 1024), gen=(32, 512), sample=True, log_prompt=False,
+                      label="config3: SmolLM2-1.7B-shape, Q5_0 attention / Q4_K FFN, 64 concurrent sessions per GPU, "
+                            "prompts uniform in [16,1024], generations uniform in [32,512], top-p 0.9 with a "
+                            "per-session seed, continuous batching")
+WORKLOADS["c4"] = dict(cfg=4, sessions=256, prompt=(32, 8192), gen=(256, 256), sample=False, log_prompt=True,
+                      label="config4: SmolLM3-3B-shape, Q4_K + Q8_0 head, 256 concurrent sessions partitioned over "
+                            "the GPUs, prompts log-uniform in [32,8192], 256 greedy decode tokens each")
+
 GEMV_M, GEMV_K = 11008, 2048
+
+
+def run_batched(args, rank, world, local, barrier):
+    """Configs 3 and 4: many ragged sessions at once through cmol_generate_batch
+    (one request per session, continuous batching on each GPU).  value =
+    generated tokens of all ranks / max over ranks of the device time of all
+    steps (prefill steps included); e2e = the same tokens over the wall time
+    of the cmol_generate_batch call (host buffers)."""
+    import numpy as np
+
+    from libcmol_b200 import synth
+    from libcmol_b200.model import GenParams, Model
+    wl = WORKLOADS[args.workload]
+    sessions = wl["sessions"] if wl["cfg"] == 3 else max(1, sessions_per_rank(wl["sessions"], world, rank))
+    if args.sessions > 0:
+        sessions = args.sessions
+    rng = np.random.default_rng(1000 * wl["cfg"] + rank)
+    lo, hi = wl["prompt"]
+    if wl["log_prompt"]:
+        plen = np.exp(rng.uniform(np.log(lo), np.log(hi), sessions)).astype(int)
+    else:
+        plen = rng.integers(lo, hi + 1, sessions)
+    glen = rng.integers(wl["gen"][0], wl["gen"][1] + 1, sessions)
+    if args.prompt_scale != 1.0:
+        plen = np.maximum(1, (plen * args.prompt_scale).astype(int))
+    ctx = int(plen.max() + glen.max() + 8)
+    spec = synth.baseline_spec(wl["cfg"], ctx=max(ctx, 256))
+    path = ensure_model(spec, rank, barrier)
+    V = spec.vocab_size
+    prompts = [rng.integers(0, V, int(n)).astype(np.int32) for n in plen]
+    params = [GenParams.make(0.9 if wl["sample"] else 0.0, top_p=0.9, top_k=40, seed=1 + i,
+                             repeat_penalty=1.0, max_new_tokens=int(g)) for i, g in enumerate(glen)]
+    with Model(path, max_ctx=ctx, max_sessions=sessions, devices=[local]) as m:
+        ss = [m.acquire() for _ in range(sessions)]
+        # warm-up: every session one short request (captures the wide buckets)
+        warm = [GenParams.make(0.0, max_new_tokens=args.warmup) for _ in ss]
+        m.generate_batch(ss, [p[:2] for p in prompts], warm)
+        for s in ss:
+            s.reset()
+        clocks = Clocks(local)
+        clocks.start()
+        barrier()
+        m.reset_stats()
+        t0 = time.perf_counter()
+        outs = m.generate_batch(ss, prompts, params)
+        t1 = time.perf_counter()
+        barrier()
+        clocks.stop()
+        st = m.stats(0)
+        gen = int(sum(len(o) for o in outs))
+        dev_ms, wall_ms, steps = st.step_ms_total, (t1 - t0) * 1000.0, st.steps
+        launches = st.kernel_launches_per_step
+        for s in ss:
+            s.release()
+    import torch.distributed as tdist
+    (gen_all, prefill_all), (dev_ms, wall_ms, steps) = reduce_ranks(
+        tdist if world > 1 else None, f"cuda:{local}", sums=(gen, int(plen.sum())), maxes=(dev_ms, wall_ms, steps))
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    print(json.dumps({
+        "metric": "decode tokens/sec (aggregate over GPUs)", "value": round(gen_all / (dev_ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": int(steps), "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / max(1.0, steps), 4), "higher_is_better": True,
+        "scaling": "strong" if wl["cfg"] == 4 else "weak", "vs_baseline": None, "dtype": "f32 (f16 tensor-core products)",
+        "data": "synthetic",
+        "config": {"workload": wl["label"], "model": spec.name, "sessions_per_gpu": sessions,
+                   "generated_tokens": int(gen_all), "prompt_tokens": int(prefill_all),
+                   "prompt_scale": args.prompt_scale,
+                   "note": "prompts run through the decode step one token per session per step"},
+        "e2e": {"value": round(gen_all / (wall_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * (4 * sessions + 1 + 3 * sessions), "d2h_bytes_per_step": 4 * (sessions + 1)},
+        "prefill_tokens_per_s": round(prefill_all / (dev_ms / 1e3), 1),
+        "gpu_launches": int(steps * launches),
+        "clocks": clocks.summary(),
+        "peak_source": peak_kind,
+    }), flush=True)
 
 
 def run_gemv_microbench(args, rank, local):
@@ -57,7 +142,7 @@ def run_gemv_microbench(args, rank, local):
     import numpy as np
     import torch
 
-    from libcmol_b200 import Weight, gemv_bench, synth
+    from libcmol_b200 import Weight, gemv_bench, matmul_batched_bench, synth
     if rank != 0:
         return
     torch.cuda.set_device(local)
@@ -70,13 +155,19 @@ def run_gemv_microbench(args, rank, local):
         ncopy = max(2, int(2 * 2 * 126e6 // nbytes) + 1)
         ws = [Weight(blob, dt, GEMV_M, GEMV_K) for _ in range(ncopy)]
         row = {}
-        for n in (1, 2):
+        for n in (1, 2, 4, 8, 16, 32, 64, 128):
             x = torch.randn(n, GEMV_K, device=f"cuda:{local}")
             y = torch.zeros(n, GEMV_M, device=f"cuda:{local}")
-            gemv_bench(ws, x, y, n, iters=2 * ncopy, reps=2)              # warm-up
-            ms = gemv_bench(ws, x, y, n, iters=4 * ncopy, reps=max(3, args.steps // 16))
+            tc = n >= 4 and dt in (synth.Q4_K, synth.Q8_0, synth.Q4_0, synth.Q5_0)
+            if n > 2 and not tc:
+                continue
+            fn = matmul_batched_bench if tc else gemv_bench
+            fn(ws, x, y, n, iters=2 * ncopy, reps=2)                      # warm-up
+            ms = fn(ws, x, y, n, iters=4 * ncopy, reps=max(3, args.steps // 16))
             gbs = nbytes / (ms * 1e-3) / 1e9
-            row[str(n)] = {"us": round(ms * 1e3, 3), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4)}
+            tfs = 2.0 * GEMV_M * GEMV_K * n / (ms * 1e-3) / 1e12
+            row[str(n)] = {"path": "tcgen05" if tc else "gemv", "us": round(ms * 1e3, 3), "GBps": round(gbs, 1),
+                           "frac": round(gbs / peak, 4), "TFLOPs": round(tfs, 2)}
         res[synth.DTYPE_NAMES[dt]] = {"bytes": nbytes, "copies": ncopy, "n": row}
         for w in ws:
             w.free()
@@ -97,6 +188,30 @@ def env_int(name, default):
         return int(os.environ.get(name, default))
     except ValueError:
         return default
+
+
+def reduce_ranks(dist, device, sums=(), maxes=()):
+    """Sum `sums` and take the max of `maxes` over all ranks; every rank gets
+    both lists back.  The whole-job numbers: tokens add up over the GPUs,
+    time is the slowest rank's device time."""
+    sums, maxes = [float(v) for v in sums], [float(v) for v in maxes]
+    if dist is None or not dist.is_initialized() or dist.get_world_size() < 2:
+        return sums, maxes
+    import torch
+    out = []
+    for vals, op in ((sums, dist.ReduceOp.SUM), (maxes, dist.ReduceOp.MAX)):
+        if vals:
+            t = torch.tensor(vals, dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=op)
+            vals = [float(v) for v in t.tolist()]
+        out.append(vals)
+    return out[0], out[1]
+
+
+def sessions_per_rank(total, world, rank):
+    """Sessions of one rank when `total` sessions are partitioned over `world`
+    GPUs (the first total % world ranks take one more)."""
+    return total // world + (1 if rank < total % world else 0)
 
 
 def model_path(spec):
@@ -285,6 +400,8 @@ def main():
     ap.add_argument("--ref-prompt", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (profiling runs)")
+    ap.add_argument("--sessions", type=int, default=0, help="override the session count (c3/c4)")
+    ap.add_argument("--prompt-scale", type=float, default=1.0, help="scale the c3/c4 prompt lengths (short runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -310,6 +427,11 @@ def main():
         return
     if args.workload == "c5":
         run_gemv_microbench(args, rank, local)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    if args.workload in ("c3", "c4"):
+        run_batched(args, rank, world, local, barrier)
         if dist is not None:
             dist.destroy_process_group()
         return
@@ -354,11 +476,7 @@ def main():
         sweep_ms, sweep_bytes, sweep_launches = m.gemv_sweep(0, reps=20)
         s.release()
 
-    if dist is not None:
-        import torch
-        t = torch.tensor([dev_ms, wall_ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_ms, wall_ms = float(t[0]), float(t[1])
+    _, (dev_ms, wall_ms) = reduce_ranks(dist, f"cuda:{local}", maxes=(dev_ms, wall_ms))
 
     if rank == 0:
         n = world

@@ -92,6 +92,8 @@ typedef struct {
     long long kv_bytes_read;     /* KV bytes the attention read (sum)     */
     int       kernel_launches_per_step;
     int       graph_steps;       /* steps run through a CUDA graph        */
+    long long steps;             /* all steps (prefill, decode and mixed) */
+    double    step_ms_total;     /* device time of all steps              */
 } cmol_cuda_stats_t;
 
 cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats_t *out);

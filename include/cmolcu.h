@@ -84,6 +84,13 @@ int cmolcu_gemv(const cmolcu_weight_t *w,
 int cmolcu_matmul_batched(const cmolcu_weight_t *w, const float *x, int n, const float *norm_w, float eps,
                           float *y, void *stream);
 
+/* Microbenchmark of the tensor-core path: `iters` back-to-back
+ * cmolcu_matmul_batched products (rotating over the nw weights of one
+ * shape, n <= 256 columns, x [n][k], y [n][rows] on the device) captured in
+ * one CUDA graph and replayed `reps` times; device time per product. */
+int cmolcu_matmul_batched_bench(cmolcu_weight_t *const *ws, int nw, const float *x, int n, float *y,
+                                int iters, int reps, float *ms_per_matmul);
+
 /* Microbenchmark: `iters` back-to-back GEMVs (rotating over the nw weights,
  * all of one shape, n = 1 or 2 columns, x [n][k], y [n][rows] on the
  * device), captured once in a CUDA graph with programmatic dependent launch

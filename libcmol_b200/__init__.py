@@ -67,6 +67,8 @@ def _declare(L):
                                  _vp, C.c_longlong, C.c_int, _vp])
     sig("cmolcu_matmul", None, [_fp, _vp, _fp, C.c_int, C.c_int, C.c_int, C.c_int])
     sig("cmolcu_matmul_batched", C.c_int, [_vp, _vp, C.c_int, _vp, C.c_float, _vp, _vp])
+    sig("cmolcu_matmul_batched_bench", C.c_int, [C.POINTER(_vp), C.c_int, _vp, C.c_int, _vp, C.c_int, C.c_int,
+                                                 C.POINTER(C.c_float)])
     sig("cmolcu_fault_status", C.c_int, [C.c_int, C.POINTER(C.c_uint), C.c_int])
     sig("cmolcu_gemv_bench", C.c_int, [C.POINTER(_vp), C.c_int, _vp, C.c_int, _vp, C.c_int, C.c_int,
                                        C.POINTER(C.c_float)])
@@ -122,6 +124,15 @@ class Weight:
         check(lib().cmolcu_matmul_batched(self.h, x.data_ptr(), n,
                                           norm_w.data_ptr() if norm_w is not None else None, eps,
                                           y.data_ptr(), stream), "cmolcu_matmul_batched")
+
+
+def matmul_batched_bench(weights, x, y, n: int, iters: int = 64, reps: int = 5) -> float:
+    """Device milliseconds per tensor-core product over back-to-back launches."""
+    arr = (_vp * len(weights))(*[w.h for w in weights])
+    ms = C.c_float(0)
+    check(lib().cmolcu_matmul_batched_bench(arr, len(weights), x.data_ptr(), n, y.data_ptr(), iters, reps,
+                                            C.byref(ms)), "cmolcu_matmul_batched_bench")
+    return ms.value
 
 
 def gemv_bench(weights, x, y, n: int, iters: int = 64, reps: int = 5) -> float:

@@ -691,6 +691,8 @@ extern "C" cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int g, cmol_cuda_st
     out->weight_bytes = e->weight_bytes_per_step();
     out->kernel_launches_per_step = e->stats.launches_per_step;
     out->graph_steps = (int)e->stats.graph_steps;
+    out->steps = e->stats.steps;
+    out->step_ms_total = e->stats.step_ms_total;
     return CMOL_OK;
 }
 

@@ -7,6 +7,7 @@
 #define TC_DQW 8                          // dequantising warps (2..9)
 #define TC_THREADS ((2 + TC_DQW) * 32)    // + producer warp 0, MMA warp 1
 #define TC_DQT (TC_DQW * 32)
+#define TC_MAX_DEPTH 8
 
 bool tc_supported(int dt) { return dt == DT_Q4_K || dt == DT_Q8_0 || dt == DT_Q4_0 || dt == DT_Q5_0; }
 
@@ -118,13 +119,26 @@ struct TcParams {
     int            *counters;
     int             q_off[4];          // plane offsets in the quantised stage (TC_M rows of a full K-chunk each)
     uint32_t        tmem_cols;
+    int             depth;             // A / B tile ring depth (<= TC_MAX_DEPTH)
 };
 
 // 16 dequantised values of row r, values [v, v + 16) of the K-chunk held in
-// the quantised stage (GGUF block arithmetic of src/quant.c:152-194).
+// the quantised stage (GGUF block arithmetic of src/quant.c:152-194), as 8
+// packed f16 pairs.  No conversion instructions: a small unsigned integer u
+// becomes the f16 1024 + u by placing it under the exponent bits 0x6400
+// (one byte permute per pair), and the f32 2^23 + u under 0x4B000000.
+//   Q8_0, Q4_0, Q5_0: q is exact in f16 and the block scale d is an f16, so
+//                     d * q in f16 arithmetic is the f16 rounding of the exact
+//                     value (the same as rounding the f32 product).
+//   Q4_K:             d * sc * q - dmin * mn in f32 (sc, mn 6-bit), then f16.
+__device__ __forceinline__ uint32_t h2_from_bytes(uint32_t w, uint32_t sel) {
+    // bytes of w selected by sel into the low byte of each half, 0x64 above
+    return __byte_perm(w, 0x64646464u, sel);
+}
+
 template <int DT>
 __device__ __forceinline__ void tc_dequant16(const uint8_t *q, const int *q_off, const int *st, int r, int v,
-                                             float out[16]) {
+                                             uint32_t out[8]) {
     const uint8_t *P0 = q + q_off[0] + r * st[0];
     const uint8_t *P1 = q + q_off[1] + r * st[1];
     if constexpr (DT == DT_Q4_K) {
@@ -137,32 +151,49 @@ __device__ __forceinline__ void tc_dequant16(const uint8_t *q, const int *q_off,
         const float a = d * (half ? sc1 : sc0), m = dmin * (half ? mn1 : mn0);
         const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const uint32_t b = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-            const float nib = (float)(half ? (b >> 4) : (b & 15u));
-            out[i] = __fmaf_rn(a, nib, -m);
+        for (int i = 0; i < 4; i++) {
+            const uint32_t t = half ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
+            float f[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                f[j] = __fmaf_rn(a, __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7540u | j)) - 8388608.0f, -m);
+            out[2 * i] = pack_h2(f[0], f[1]);
+            out[2 * i + 1] = pack_h2(f[2], f[3]);
         }
-    } else if constexpr (DT == DT_Q8_0) {
+    } else {
         const int b = v >> 5, hh = (v >> 4) & 1;
-        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 32 + 16 * hh);
-        const float d = h2f(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
-        const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
+        uint32_t w[4];
+        __half bias;
+        __half d;
+        if constexpr (DT == DT_Q8_0) {
+            const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 32 + 16 * hh);
+            d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
+            w[0] = pl.x ^ 0x80808080u; w[1] = pl.y ^ 0x80808080u;      // int8 -> unsigned + 128
+            w[2] = pl.z ^ 0x80808080u; w[3] = pl.w ^ 0x80808080u;
+            bias = __ushort_as_half((uint16_t)0x6480);                  // 1024 + 128
+        } else {
+            const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 16);
+            d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
+            const uint32_t raw[4] = {pl.x, pl.y, pl.z, pl.w};
 #pragma unroll
-        for (int i = 0; i < 16; i++) out[i] = d * (float)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFFu);
-    } else {   // Q4_0, Q5_0
-        const int b = v >> 5, hh = (v >> 4) & 1;
-        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 16);
-        const float d = h2f(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
-        uint32_t qh = 0;
-        if constexpr (DT == DT_Q5_0) qh = *reinterpret_cast<const uint32_t *>(q + q_off[2] + r * st[2] + b * 4);
-        const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
+            for (int i = 0; i < 4; i++) w[i] = hh ? ((raw[i] >> 4) & 0x0F0F0F0Fu) : (raw[i] & 0x0F0F0F0Fu);
+            if constexpr (DT == DT_Q5_0) {
+                const uint32_t qh = *reinterpret_cast<const uint32_t *>(q + q_off[2] + r * st[2] + b * 4);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-            int nib = (int)(hh ? (byte >> 4) : (byte & 15u));
-            if constexpr (DT == DT_Q5_0) nib = (nib | (int)(((qh >> (16 * hh + i)) & 1u) << 4)) - 16;
-            else nib -= 8;
-            out[i] = d * (float)nib;
+                for (int i = 0; i < 4; i++) w[i] |= spread4_bit4((qh >> (16 * hh + 4 * i)) & 15u);
+                bias = __ushort_as_half((uint16_t)0x6410);              // 1024 + 16
+            } else {
+                bias = __ushort_as_half((uint16_t)0x6408);              // 1024 + 8
+            }
+        }
+        const __half2 b2 = __halves2half2(bias, bias), d2 = __halves2half2(d, d);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t lo = h2_from_bytes(w[i], 0x5140u), hi = h2_from_bytes(w[i], 0x5342u);
+            __half2 x0 = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), b2), d2);
+            __half2 x1 = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), b2), d2);
+            out[2 * i] = *reinterpret_cast<const uint32_t *>(&x0);
+            out[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&x1);
         }
     }
 }
@@ -201,20 +232,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
 
     // shared memory: A tiles, B tiles, quantised stage (all 1024-aligned), then barriers
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
-    uint8_t *A = base;                                        // 2 x 16 KB
-    uint8_t *B = A + 2 * TC_M * 128;                          // 2 x npad * 128
-    uint8_t *Q = B + 2 * (size_t)npad * 128;                  // quantised K-chunk
+    const int D = p.depth;
+    uint8_t *A = base;                                        // D x 16 KB
+    uint8_t *B = A + (size_t)D * TC_M * 128;                  // D x npad * 128
+    uint8_t *Q = B + (size_t)D * npad * 128;                  // quantised K-chunk
     const int qbytes = p.q_off[3] + TC_M * (w.nplanes > 3 ? w.cs[3] : 0);
     uint64_t *bars = reinterpret_cast<uint64_t *>(Q + ((qbytes + 127) & ~127));
-    uint64_t *qfull = bars, *qempty = bars + 1, *afull = bars + 2, *aempty = bars + 4, *bfull = bars + 6,
-             *bempty = bars + 8, *accfull = bars + 10;
+    uint64_t *qfull = bars, *qempty = bars + 1, *accfull = bars + 2, *afull = bars + 3,
+             *aempty = afull + TC_MAX_DEPTH, *bfull = aempty + TC_MAX_DEPTH, *bempty = bfull + TC_MAX_DEPTH;
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
 
     if (tid == 0) {
         mbar_init(qfull, 1);
         mbar_init(qempty, TC_DQW);
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < D; i++) {
             mbar_init(&afull[i], TC_DQW);
             mbar_init(&aempty[i], 1);
             mbar_init(&bfull[i], 1);
@@ -257,7 +289,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
                 const int g0 = (j * w.kc) / TC_KB;
                 bool ok = true;
                 for (int i = 0; i < kbs; i++, bn++) {
-                    const int slot = bn & 1, use = bn >> 1;
+                    const int slot = bn % D, use = bn / D;
                     if (use > 0 && !mbar_wait(&bempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
                     mbar_arrive_expect_tx(&bfull[slot], (uint32_t)(npad * 128));
                     bulk_g2s(B + (size_t)slot * npad * 128, p.xs + (size_t)(g0 + i) * npad * 64, (uint32_t)(npad * 128),
@@ -271,7 +303,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | ((uint32_t)(npad >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
             for (int i = 0; i < nkb; i++) {
-                const int slot = i & 1, use = i >> 1;
+                const int slot = i % D, use = i / D;
                 mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
                 mbar_wait(&bfull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
                 tc_fence_after();
@@ -296,19 +328,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
             for (int pl = 0; pl < 4; pl++) st[pl] = qw_stride(w, pl, j);
             const int kbs = qw_chunk_values(w, j) / TC_KB;
             for (int ib = 0; ib < kbs; ib++, i++) {
-                const int slot = i & 1, use = i >> 1;
+                const int slot = i % D, use = i / D;
                 if (use > 0) mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY);
                 uint8_t *tile = A + slot * TC_M * 128;
                 // task = (row r, 16-value run q): 128 rows x 4 runs
 #pragma unroll
                 for (int t = 0; t < (TC_M * 4) / TC_DQT; t++) {
                     const int task = dt + TC_DQT * t, r = task >> 2, q = task & 3;
-                    float v[16];
-                    tc_dequant16<DT>(Q, p.q_off, st, r, ib * TC_KB + 16 * q, v);
-                    const uint4 lo = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
-                                                pack_h2(v[6], v[7]));
-                    const uint4 hi = make_uint4(pack_h2(v[8], v[9]), pack_h2(v[10], v[11]), pack_h2(v[12], v[13]),
-                                                pack_h2(v[14], v[15]));
+                    uint32_t h[8];
+                    tc_dequant16<DT>(Q, p.q_off, st, r, ib * TC_KB + 16 * q, h);
+                    const uint4 lo = make_uint4(h[0], h[1], h[2], h[3]);
+                    const uint4 hi = make_uint4(h[4], h[5], h[6], h[7]);
                     uint4 *row = reinterpret_cast<uint4 *>(tile + r * 128);
                     row[(2 * q) ^ (r & 7)] = lo;
                     row[(2 * q + 1) ^ (r & 7)] = hi;
@@ -391,7 +421,7 @@ static int tc_npad(int ncol) { return std::max(16, (ncol + 15) / 16 * 16); }
 static void tc_split(int rows, int nkc, int &rblocks, int &ksplit, int &cps) {
     const int sms = device_sm_count();
     rblocks = (rows + TC_M - 1) / TC_M;
-    ksplit = std::max(1, std::min(nkc, (sms + rblocks - 1) / rblocks));
+    ksplit = std::max(1, std::min(nkc, sms / rblocks));   // one wave: at most one CTA per SM
     cps = (nkc + ksplit - 1) / ksplit;
     ksplit = (nkc + cps - 1) / cps;
 }
@@ -446,7 +476,11 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
         off += pl < w.nplanes ? TC_M * w.cs[pl] : 0;
     }
     p.tmem_cols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
-    const size_t smem = 1024 + 2 * TC_M * 128 + 2 * (size_t)npad * 128 + (((size_t)off + 127) & ~(size_t)127) + 16 * 8;
+    const size_t qb = ((size_t)off + 127) & ~(size_t)127, bars = (3 + 4 * TC_MAX_DEPTH) * 8;
+    const size_t per_slot = (size_t)TC_M * 128 + (size_t)npad * 128;
+    const long long room = 224LL * 1024 - 1024 - (long long)qb - (long long)bars;
+    p.depth = (int)std::max<long long>(2, std::min<long long>(TC_MAX_DEPTH, room / (long long)per_slot));
+    const size_t smem = 1024 + (size_t)p.depth * per_slot + qb + bars;
     static size_t attr_done[64][4];
     int dev = 0;
     cudaGetDevice(&dev);

@@ -211,6 +211,78 @@ extern "C" int cmolcu_matmul_batched(const cmolcu_weight_t *w, const float *x, i
     return 0;
 }
 
+// Back-to-back tensor-core matmuls over `nw` distinct weights (one shape),
+// n columns, captured once in a CUDA graph (two launches each) and replayed
+// `reps` times; *ms_per_matmul from CUDA events on the replay stream.
+extern "C" int cmolcu_matmul_batched_bench(cmolcu_weight_t *const *ws, int nw, const float *x, int n, float *y,
+                                           int iters, int reps, float *ms_per_matmul) {
+    if (!ws || nw <= 0 || !x || !y || n < 1 || n > TC_MAX_N || iters <= 0 || reps <= 0 || !ms_per_matmul) {
+        cmolcu_set_error("cmolcu_matmul_batched_bench: bad arguments");
+        return -1;
+    }
+    if (!tc_supported(ws[0]->w.dtype)) { cmolcu_set_error("cmolcu_matmul_batched_bench: dtype has no tensor-core path"); return -1; }
+    const int dev = ws[0]->device;
+    CUDA_TRY(cudaSetDevice(dev));
+    size_t xh = 0, pf = 0;
+    int rb = 0;
+    tc_scratch_need(ws[0]->w.rows, ws[0]->w.k, n, &xh, &pf, &rb);
+    TcScratch sc = {};
+    cudaStream_t st = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    unsigned int *fw = cmolcu_fault_word(dev);
+    cudaError_t err = cudaMalloc(&sc.xs, xh * 2);
+    if (err == cudaSuccess) err = cudaMalloc(&sc.part, std::max<size_t>(pf, 1) * 4);
+    if (err == cudaSuccess) err = cudaMalloc(&sc.counters, (size_t)rb * 4);
+    if (err == cudaSuccess) err = cudaMemset(sc.counters, 0, (size_t)rb * 4);
+    sc.part_floats = pf;
+    sc.max_row_blocks = rb;
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    auto launch_all = [&]() -> cudaError_t {
+        for (int i = 0; i < iters; i++) {
+            const QWeight &q = ws[i % nw]->w;
+            GemvArgs a = {};
+            a.w = q;
+            a.x = x; a.x_ld = q.k; a.x_inc = 1;
+            a.y = y; a.y_ld = q.rows; a.y_inc = 1;
+            a.fault = fw;
+            cudaError_t e = tc_matmul(a, n, EPI_STORE, sc, st, true);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    };
+    if (err == cudaSuccess) err = launch_all();    // eager pass: kernel attributes, warm-up
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err == cudaSuccess) err = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (err == cudaSuccess) {
+        cudaError_t re = launch_all();
+        err = cudaStreamEndCapture(st, &g);
+        if (re != cudaSuccess) err = re;
+    }
+    if (err == cudaSuccess) err = cudaGraphInstantiate(&ge, g, 0);
+    if (err == cudaSuccess) err = cudaEventCreate(&e0);
+    if (err == cudaSuccess) err = cudaEventCreate(&e1);
+    if (err == cudaSuccess) err = cudaGraphLaunch(ge, st);
+    if (err == cudaSuccess) err = cudaEventRecord(e0, st);
+    for (int r = 0; err == cudaSuccess && r < reps; r++) err = cudaGraphLaunch(ge, st);
+    if (err == cudaSuccess) err = cudaEventRecord(e1, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    float ms = 0.f;
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(sc.xs);
+    cudaFree(sc.part);
+    cudaFree(sc.counters);
+    if (err != cudaSuccess) { cmolcu_set_error("cmolcu_matmul_batched_bench: %s", cudaGetErrorString(err)); return -1; }
+    *ms_per_matmul = ms / (float)(iters * reps);
+    return 0;
+}
+
 // Back-to-back GEMVs over `nw` distinct weights (all the same shape), captured
 // in one CUDA graph with programmatic dependent launch between them, replayed
 // `reps` times; *ms_per_gemv = device time per GEMV (CUDA events).

@@ -58,7 +58,7 @@ class CudaStats(C.Structure):
                 ("prefill_tokens", C.c_longlong), ("decode_ms", C.c_double),
                 ("step_ms_last", C.c_double), ("weight_bytes", C.c_longlong),
                 ("kv_bytes_read", C.c_longlong), ("kernel_launches_per_step", C.c_int),
-                ("graph_steps", C.c_int)]
+                ("graph_steps", C.c_int), ("steps", C.c_longlong), ("step_ms_total", C.c_double)]
 
 
 class BatchItem(C.Structure):

@@ -352,7 +352,7 @@ def _gen_tensor(spec, idx, name, dtype, shape, chunk_rows):
         yield quantize(w, dtype)
 
 
-def write_gguf(path: str, spec: ModelSpec, chunk_rows: int = 4096):
+def write_gguf(path: str, spec: ModelSpec, chunk_rows: int = 4096, workers: int | None = None):
     """Write the synthetic model; returns path.  Deterministic in spec.seed."""
     arch = spec.arch
     toks, scores, types, merges = synth_vocab(spec.vocab_size)
@@ -392,17 +392,44 @@ def write_gguf(path: str, spec: ModelSpec, chunk_rows: int = 4096):
     head = b"GGUF" + struct.pack("<IQQ", 3, len(plan), len(kvs)) + b"".join(kvs) + b"".join(infos)
     pad = (-len(head)) % ALIGN
     tmp = path + ".tmp"
+    data0 = len(head) + pad
     with open(tmp, "wb") as f:
         f.write(head + b"\0" * pad)
-        for idx, (name, dt, shape) in enumerate(plan):
-            n = 0
-            for blk in _gen_tensor(spec, idx, name, dt, shape, chunk_rows):
-                b = blk.tobytes()
-                f.write(b)
-                n += len(b)
-            f.write(b"\0" * ((-n) % ALIGN))
+        f.truncate(data0 + off)
+    offs, o = [], 0
+    for name, dt, (rows, k) in plan:
+        offs.append(o)
+        o += (rows * row_bytes(k, dt) + ALIGN - 1) // ALIGN * ALIGN
+    jobs = [(tmp, data0 + offs[i], spec, i, name, dt, shape, chunk_rows) for i, (name, dt, shape) in enumerate(plan)]
+    if workers is None:
+        workers = min(16, os.cpu_count() or 1) if off > (256 << 20) else 1
+    done = False
+    if workers > 1:
+        # tensors are independent and seeded by index: fill them in parallel
+        # (fresh "spawn" workers, never a fork of a process that may hold a GPU
+        # context).  A pool that cannot start (e.g. a main module read from
+        # stdin cannot be re-imported by spawn) raises; fall back to serial.
+        import concurrent.futures as cf
+        import multiprocessing as mp
+        try:
+            with cf.ProcessPoolExecutor(workers, mp_context=mp.get_context("spawn")) as ex:
+                for f in [ex.submit(_write_tensor, *j) for j in jobs]:
+                    f.result(timeout=3600)
+            done = True
+        except Exception:
+            done = False
+    if not done:
+        for j in jobs:
+            _write_tensor(*j)
     os.replace(tmp, path)
     return path
+
+
+def _write_tensor(tmp, at, spec, idx, name, dt, shape, chunk_rows):
+    with open(tmp, "r+b") as f:
+        f.seek(at)
+        for blk in _gen_tensor(spec, idx, name, dt, shape, chunk_rows):
+            f.write(blk.tobytes())
 
 
 def ensure_gguf(path: str, spec: ModelSpec):
