@@ -56,6 +56,16 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 16-byte asynchronous copy global -> shared through the load/store unit,
+// and the arrival of this thread on `bar` once its earlier copies landed
+// (the mbarrier counts one arrival per issuing thread).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
@@ -110,17 +120,50 @@ __global__ void __launch_bounds__(256) k_tc_xprep(const float *x, long long x_ld
 // ---------------------------------------------------------------------------
 // The matmul
 // ---------------------------------------------------------------------------
+#define TC_SV 256          // values per quantised slice (one K-slice of 128 rows in a stage)
+#define TC_MAX_QD 4        // quantised-stage ring depth
+
 struct TcParams {
     GemvArgs        g;                 // weight, y, epilogue fields
     int             epi, ncol, npad;
     const uint16_t *xs;
-    int             ksplit, chunks_per_split;
+    int             nslice;            // K-slices of the matrix (slices never cross a K-chunk)
+    int             ksplit, slices_per_split;
     float          *part;
     int            *counters;
-    int             q_off[4];          // plane offsets in the quantised stage (TC_M rows of a full K-chunk each)
     uint32_t        tmem_cols;
     int             depth;             // A / B tile ring depth (<= TC_MAX_DEPTH)
+    int             qdepth;            // quantised-stage ring depth (<= TC_MAX_QD)
 };
+
+// Row stride, in a quantised stage, of plane p of format DT for one 256-value
+// slice: the slice's bytes rounded to 16, then to an odd multiple of 16 so
+// that the 8 lanes of a shared-memory phase reading 8 consecutive rows hit 8
+// different 16-byte bank groups.
+__host__ __device__ constexpr int tc_sp(int dt, int p) {
+    const int b = dt == DT_Q8_0 ? (p == 0 ? 256 : p == 1 ? 16 : 0)
+                : dt == DT_Q5_0 ? (p == 0 ? 128 : p == 1 ? 16 : p == 2 ? 32 : 0)
+                : (p == 0 ? 128 : p == 1 ? 16 : 0);          // Q4_0, Q4_K
+    return b == 0 ? 0 : ((b / 16) % 2 == 0 ? b + 16 : b);
+}
+__host__ __device__ constexpr int tc_stage_bytes(int dt) {
+    return TC_M * (tc_sp(dt, 0) + tc_sp(dt, 1) + tc_sp(dt, 2));
+}
+
+// Slice t of the matrix: K-chunk j, value offset `off` in it, `len` values.
+__host__ __device__ inline void tc_slice(const QWeight &w, int t, int &j, int &off, int &len) {
+    const int spc = w.kc / TC_SV;                      // slices of a full K-chunk (kc is a multiple of 256 if nkc > 1)
+    const int full = (w.nkc - 1) * spc;
+    if (t < full) {
+        j = t / spc;
+        off = (t % spc) * TC_SV;
+        len = TC_SV;
+    } else {
+        j = w.nkc - 1;
+        off = (t - full) * TC_SV;
+        len = min(TC_SV, qw_chunk_values(w, j) - off);
+    }
+}
 
 // 16 dequantised values of row r, values [v, v + 16) of the K-chunk held in
 // the quantised stage (GGUF block arithmetic of src/quant.c:152-194), as 8
@@ -137,14 +180,13 @@ __device__ __forceinline__ uint32_t h2_from_bytes(uint32_t w, uint32_t sel) {
 }
 
 template <int DT>
-__device__ __forceinline__ void tc_dequant16(const uint8_t *q, const int *q_off, const int *st, int r, int v,
+__device__ __forceinline__ void tc_dequant16(const uint8_t *P0, const uint8_t *P1, const uint8_t *P2, int v,
                                              uint32_t out[8]) {
-    const uint8_t *P0 = q + q_off[0] + r * st[0];
-    const uint8_t *P1 = q + q_off[1] + r * st[1];
     if constexpr (DT == DT_Q4_K) {
-        const int s = v >> 8, o = v & 255, pj = o >> 6, half = (o >> 5) & 1, sub = (o >> 4) & 1;
-        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + s * 128 + 32 * pj + 16 * sub);
-        const uint4 h = *reinterpret_cast<const uint4 *>(P1 + s * 16);
+        // one super-block per slice: v in [0, 256)
+        const int pj = v >> 6, half = (v >> 5) & 1, sub = (v >> 4) & 1;
+        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + 32 * pj + 16 * sub);
+        const uint4 h = *reinterpret_cast<const uint4 *>(P1);
         const float d = h2f((uint16_t)(h.x & 0xFFFF)), dmin = h2f((uint16_t)(h.x >> 16));
         float sc0, sc1, mn0, mn1;
         q4k_pair(h.y, h.z, h.w, pj, sc0, sc1, mn0, mn1);
@@ -178,7 +220,7 @@ __device__ __forceinline__ void tc_dequant16(const uint8_t *q, const int *q_off,
 #pragma unroll
             for (int i = 0; i < 4; i++) w[i] = hh ? ((raw[i] >> 4) & 0x0F0F0F0Fu) : (raw[i] & 0x0F0F0F0Fu);
             if constexpr (DT == DT_Q5_0) {
-                const uint32_t qh = *reinterpret_cast<const uint32_t *>(q + q_off[2] + r * st[2] + b * 4);
+                const uint32_t qh = *reinterpret_cast<const uint32_t *>(P2 + b * 4);
 #pragma unroll
                 for (int i = 0; i < 4; i++) w[i] |= spread4_bit4((qh >> (16 * hh + 4 * i)) & 15u);
                 bias = __ushort_as_half((uint16_t)0x6410);              // 1024 + 16
@@ -222,30 +264,33 @@ __device__ __forceinline__ void tc_epilogue(const TcParams &p, int row, int col,
 }
 
 template <int DT>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant__ TcParams p) {
     const QWeight &w = p.g.w;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rb = blockIdx.x, ks = blockIdx.y;
     const int m0 = rb * TC_M;
     const int npad = p.npad;
-    const int j0 = ks * p.chunks_per_split, j1 = min(w.nkc, j0 + p.chunks_per_split);
+    const int s0 = ks * p.slices_per_split, s1 = min(p.nslice, s0 + p.slices_per_split);
+    constexpr int SP0 = tc_sp(DT, 0), SP1 = tc_sp(DT, 1), SP2 = tc_sp(DT, 2);
+    constexpr int QOFF1 = TC_M * SP0, QOFF2 = TC_M * (SP0 + SP1), QB = tc_stage_bytes(DT);
 
-    // shared memory: A tiles, B tiles, quantised stage (all 1024-aligned), then barriers
+    // shared memory: A tiles, B tiles (1024-aligned), quantised stages, barriers
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
-    const int D = p.depth;
+    const int D = p.depth, QD = p.qdepth;
     uint8_t *A = base;                                        // D x 16 KB
     uint8_t *B = A + (size_t)D * TC_M * 128;                  // D x npad * 128
-    uint8_t *Q = B + (size_t)D * npad * 128;                  // quantised K-chunk
-    const int qbytes = p.q_off[3] + TC_M * (w.nplanes > 3 ? w.cs[3] : 0);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(Q + ((qbytes + 127) & ~127));
-    uint64_t *qfull = bars, *qempty = bars + 1, *accfull = bars + 2, *afull = bars + 3,
+    uint8_t *Q = B + (size_t)D * npad * 128;                  // QD x QB
+    uint64_t *bars = reinterpret_cast<uint64_t *>(Q + (size_t)QD * QB);
+    uint64_t *accfull = bars, *qfull = bars + 1, *qempty = qfull + TC_MAX_QD, *afull = qempty + TC_MAX_QD,
              *aempty = afull + TC_MAX_DEPTH, *bfull = aempty + TC_MAX_DEPTH, *bempty = bfull + TC_MAX_DEPTH;
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
 
     if (tid == 0) {
-        mbar_init(qfull, 1);
-        mbar_init(qempty, TC_DQW);
+        for (int i = 0; i < QD; i++) {
+            mbar_init(&qfull[i], 32);       // one cp.async arrival per producer lane
+            mbar_init(&qempty[i], TC_DQW);
+        }
         for (int i = 0; i < D; i++) {
             mbar_init(&afull[i], TC_DQW);
             mbar_init(&aempty[i], 1);
@@ -267,36 +312,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
     const uint32_t tmem = s_tmem;
     pdl_launch_dependents();
 
-    // k-blocks of this CTA: every K-chunk holds a whole number of them
+    // k-blocks of this CTA (every slice holds a whole number of them)
     int nkb = 0;
-    for (int j = j0; j < j1; j++) nkb += qw_chunk_values(w, j) / TC_KB;
+    for (int t = s0; t < s1; t++) {
+        int j, off, len;
+        tc_slice(w, t, j, off, len);
+        nkb += len / TC_KB;
+    }
 
     if (warp == 0) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            const int nrow = min(TC_M, w.prow - m0);
-            int bn = 0;
-            for (int j = j0; j < j1; j++) {
-                const int qi = j - j0;
-                if (qi > 0 && !mbar_wait(qempty, (qi - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) break;
-                int bytes = 0;
-                for (int pl = 0; pl < w.nplanes; pl++) bytes += nrow * qw_stride(w, pl, j);
-                mbar_arrive_expect_tx(qfull, (uint32_t)bytes);
-                for (int pl = 0; pl < w.nplanes; pl++)
-                    bulk_g2s(Q + p.q_off[pl], qw_row(w, pl, j, m0), (uint32_t)(nrow * qw_stride(w, pl, j)), qfull);
-                if (qi == 0) pdl_wait();   // the activation image comes from the previous kernel
-                const int kbs = qw_chunk_values(w, j) / TC_KB;
-                const int g0 = (j * w.kc) / TC_KB;
-                bool ok = true;
-                for (int i = 0; i < kbs; i++, bn++) {
-                    const int slot = bn % D, use = bn / D;
-                    if (use > 0 && !mbar_wait(&bempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
+        // ---------------- producer: quantised slices (all lanes) and activation blocks (lane 0) --------
+        const int nrow = min(TC_M, w.prow - m0);
+        int bn = 0;
+        bool ok = true;
+        for (int t = s0; t < s1 && ok; t++) {
+            const int li = t - s0, stg = li % QD, use = li / QD;
+            if (use > 0 && !mbar_wait(&qempty[stg], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
+            int j, off, len;
+            tc_slice(w, t, j, off, len);
+            // 16-byte chunks of every row of every plane (consecutive lanes take
+            // consecutive chunks of a row: coalesced reads of the K-chunk-major planes)
+            const int c0 = round16(qw_plane_bytes(DT, 0, len)) / 16;
+            const int c1 = round16(qw_plane_bytes(DT, 1, len)) / 16;
+            const int c2 = DT == DT_Q5_0 ? round16(qw_plane_bytes(DT, 2, len)) / 16 : 0;
+            const int o0 = qw_plane_bytes(DT, 0, off), o1 = qw_plane_bytes(DT, 1, off), o2 = qw_plane_bytes(DT, 2, off);
+            uint8_t *q = Q + (size_t)stg * QB;
+            for (int idx = lane; idx < nrow * c0; idx += 32) {
+                const int r = idx / c0, c = idx % c0;
+                cp_async16(q + r * SP0 + 16 * c, qw_row(w, 0, j, m0 + r) + o0 + 16 * c);
+            }
+            for (int idx = lane; idx < nrow * c1; idx += 32) {
+                const int r = idx / c1, c = idx % c1;
+                cp_async16(q + QOFF1 + r * SP1 + 16 * c, qw_row(w, 1, j, m0 + r) + o1 + 16 * c);
+            }
+            if constexpr (DT == DT_Q5_0) {
+                for (int idx = lane; idx < nrow * c2; idx += 32) {
+                    const int r = idx / c2, c = idx % c2;
+                    cp_async16(q + QOFF2 + r * SP2 + 16 * c, qw_row(w, 2, j, m0 + r) + o2 + 16 * c);
+                }
+            }
+            cp_async_arrive(&qfull[stg]);
+            if (lane == 0) {
+                if (li == 0) pdl_wait();   // the activation image comes from the previous kernel
+                const int g0 = (j * w.kc + off) / TC_KB;
+                for (int i = 0; i < len / TC_KB; i++, bn++) {
+                    const int slot = bn % D, u = bn / D;
+                    if (u > 0 && !mbar_wait(&bempty[slot], (u - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
                     mbar_arrive_expect_tx(&bfull[slot], (uint32_t)(npad * 128));
                     bulk_g2s(B + (size_t)slot * npad * 128, p.xs + (size_t)(g0 + i) * npad * 64, (uint32_t)(npad * 128),
                              &bfull[slot]);
                 }
-                if (!ok) break;
             }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
     } else if (warp == 1) {
         // ---------------- MMA issue ----------------
@@ -320,35 +387,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
         // ---------------- dequantise ----------------
         const int dt = tid - 64;
         int i = 0;
-        for (int j = j0; j < j1; j++) {
-            const int qi = j - j0;
-            mbar_wait(qfull, qi & 1, p.g.fault, FAULT_GEMV_FULL);
-            int st[4];
-#pragma unroll
-            for (int pl = 0; pl < 4; pl++) st[pl] = qw_stride(w, pl, j);
-            const int kbs = qw_chunk_values(w, j) / TC_KB;
-            for (int ib = 0; ib < kbs; ib++, i++) {
+        for (int t = s0; t < s1; t++) {
+            const int li = t - s0, stg = li % QD;
+            mbar_wait(&qfull[stg], (li / QD) & 1, p.g.fault, FAULT_GEMV_FULL);
+            int j, off, len;
+            tc_slice(w, t, j, off, len);
+            const uint8_t *q = Q + (size_t)stg * QB;
+            for (int ib = 0; ib < len / TC_KB; ib++, i++) {
                 const int slot = i % D, use = i / D;
                 if (use > 0) mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY);
                 uint8_t *tile = A + slot * TC_M * 128;
-                // task = (row r, 16-value run q): 128 rows x 4 runs
+                // task = (row r, 16-value run qq): 128 rows x 4 runs
 #pragma unroll
-                for (int t = 0; t < (TC_M * 4) / TC_DQT; t++) {
-                    const int task = dt + TC_DQT * t, r = task >> 2, q = task & 3;
+                for (int tt = 0; tt < (TC_M * 4) / TC_DQT; tt++) {
+                    const int task = dt + TC_DQT * tt, r = task >> 2, qq = task & 3;
                     uint32_t h[8];
-                    tc_dequant16<DT>(Q, p.q_off, st, r, ib * TC_KB + 16 * q, h);
-                    const uint4 lo = make_uint4(h[0], h[1], h[2], h[3]);
-                    const uint4 hi = make_uint4(h[4], h[5], h[6], h[7]);
+                    tc_dequant16<DT>(q + r * SP0, q + QOFF1 + r * SP1, q + QOFF2 + r * SP2, ib * TC_KB + 16 * qq, h);
                     uint4 *row = reinterpret_cast<uint4 *>(tile + r * 128);
-                    row[(2 * q) ^ (r & 7)] = lo;
-                    row[(2 * q + 1) ^ (r & 7)] = hi;
+                    row[(2 * qq) ^ (r & 7)] = make_uint4(h[0], h[1], h[2], h[3]);
+                    row[(2 * qq + 1) ^ (r & 7)] = make_uint4(h[4], h[5], h[6], h[7]);
                 }
                 fence_proxy_async_smem();   // the tensor core reads the tile through the async proxy
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&afull[slot]);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(qempty);
+            if (lane == 0) mbar_arrive(&qempty[stg]);
         }
         // ---------------- epilogue: tensor memory -> registers ----------------
         if (warp < 6) {
@@ -418,20 +482,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(const __grid_constant
 // ---------------------------------------------------------------------------
 static int tc_npad(int ncol) { return std::max(16, (ncol + 15) / 16 * 16); }
 
-static void tc_split(int rows, int nkc, int &rblocks, int &ksplit, int &cps) {
-    const int sms = device_sm_count();
+// Ring depths and shared memory of one CTA: two CTAs share an SM when both
+// fit (<= 112 KB each, narrow batches); otherwise one CTA takes the SM and
+// deeper rings.
+static void tc_rings(int dt, int npad, int &depth, int &qdepth, size_t &smem, int &per_sm) {
+    const size_t qb = (size_t)tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
+    const size_t per_slot = (size_t)TC_M * 128 + (size_t)npad * 128;
+    for (per_sm = 2; per_sm >= 1; per_sm--) {
+        const long long budget = per_sm == 2 ? 112LL * 1024 : 220LL * 1024;
+        qdepth = per_sm == 2 ? 2 : 3;
+        const long long room = budget - 1024 - (long long)(qdepth * qb) - (long long)bars;
+        depth = (int)std::min<long long>(TC_MAX_DEPTH, room / (long long)per_slot);
+        smem = 1024 + (size_t)std::max(depth, 2) * per_slot + (size_t)qdepth * qb + bars;
+        if (depth >= 2 && (long long)smem <= budget) return;
+    }
+    per_sm = 1;
+    depth = 2;
+    qdepth = 2;
+    smem = 1024 + 2 * per_slot + 2 * qb + bars;
+}
+
+static int tc_nslice(int k, int kc) {
+    const int nkc = (k + kc - 1) / kc;
+    const int last = k - (nkc - 1) * kc;
+    return (nkc - 1) * (kc / TC_SV) + (last + TC_SV - 1) / TC_SV;
+}
+
+static void tc_split(int rows, int nslice, int per_sm, int &rblocks, int &ksplit, int &sps) {
+    const int slots = device_sm_count() * per_sm;
     rblocks = (rows + TC_M - 1) / TC_M;
-    ksplit = std::max(1, std::min(nkc, sms / rblocks));   // one wave: at most one CTA per SM
-    cps = (nkc + ksplit - 1) / ksplit;
-    ksplit = (nkc + cps - 1) / cps;
+    ksplit = std::max(1, std::min(nslice, slots / rblocks));    // one wave
+    sps = (nslice + ksplit - 1) / ksplit;
+    ksplit = (nslice + sps - 1) / sps;
 }
 
 void tc_scratch_need(int rows, int k, int ncol, size_t *xs_halves, size_t *part_floats, int *row_blocks) {
     const int npad = tc_npad(ncol);
     *xs_halves = (size_t)k * npad;
-    // the K-chunk count is at most k / 512 + 1 for the supported formats
-    int rb, ks, cps;
-    tc_split(rows, k / 512 + 1, rb, ks, cps);
+    int rb, ks, sps;
+    tc_split(rows, k / TC_KB, 2, rb, ks, sps);     // an upper bound on the split of any format
     *part_floats = ks > 1 ? (size_t)rb * ks * npad * TC_M : 0;
     *row_blocks = rb;
 }
@@ -451,13 +540,17 @@ static tc_kernel_t tc_pick(int dt) {
 cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, cudaStream_t st, bool pdl) {
     const QWeight &w = a.w;
     tc_kernel_t k = tc_pick(w.dtype);
-    if (!k || ncol < 1 || ncol > TC_MAX_N || w.k % TC_KB || w.kc % TC_KB || a.x_inc != 1 || a.y_inc != 1)
-        return cudaErrorInvalidValue;
+    if (!k || ncol < 1 || ncol > TC_MAX_N || w.k % TC_KB || a.x_inc != 1 || a.y_inc != 1) return cudaErrorInvalidValue;
+    if (w.nkc > 1 && w.kc % TC_SV) return cudaErrorInvalidValue;
+    if (w.dtype == DT_Q4_K && w.k % TC_SV) return cudaErrorInvalidValue;
     const int npad = tc_npad(ncol);
-    int rb, ks, cps;
-    tc_split(w.rows, w.nkc, rb, ks, cps);
-    if ((size_t)w.k * npad > ((size_t)1 << 40) || !s.xs || rb > s.max_row_blocks ||
-        (ks > 1 && (size_t)rb * ks * npad * TC_M > s.part_floats))
+    int depth, qdepth, per_sm;
+    size_t smem;
+    tc_rings(w.dtype, npad, depth, qdepth, smem, per_sm);
+    const int nslice = tc_nslice(w.k, w.kc);
+    int rb, ks, sps;
+    tc_split(w.rows, nslice, per_sm, rb, ks, sps);
+    if (!s.xs || rb > s.max_row_blocks || (ks > 1 && (size_t)rb * ks * npad * TC_M > s.part_floats))
         return cudaErrorInvalidValue;
     TcParams p = {};
     p.g = a;
@@ -466,21 +559,14 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     p.ncol = ncol;
     p.npad = npad;
     p.xs = s.xs;
+    p.nslice = nslice;
     p.ksplit = ks;
-    p.chunks_per_split = cps;
+    p.slices_per_split = sps;
     p.part = s.part;
     p.counters = s.counters;
-    int off = 0;
-    for (int pl = 0; pl < 4; pl++) {
-        p.q_off[pl] = off;
-        off += pl < w.nplanes ? TC_M * w.cs[pl] : 0;
-    }
     p.tmem_cols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
-    const size_t qb = ((size_t)off + 127) & ~(size_t)127, bars = (3 + 4 * TC_MAX_DEPTH) * 8;
-    const size_t per_slot = (size_t)TC_M * 128 + (size_t)npad * 128;
-    const long long room = 224LL * 1024 - 1024 - (long long)qb - (long long)bars;
-    p.depth = (int)std::max<long long>(2, std::min<long long>(TC_MAX_DEPTH, room / (long long)per_slot));
-    const size_t smem = 1024 + (size_t)p.depth * per_slot + qb + bars;
+    p.depth = depth;
+    p.qdepth = qdepth;
     static size_t attr_done[64][4];
     int dev = 0;
     cudaGetDevice(&dev);
