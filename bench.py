@@ -57,7 +57,7 @@ WORKLOADS["c4"] = dict(cfg=4, sessions=256, prompt=(32, 8192), gen=(256, 256), s
 GEMV_M, GEMV_K = 11008, 2048
 
 
-def run_batched(args, rank, world, local, barrier):
+def run_batched(args, rank, world, local, barrier, dist=None):
     """Configs 3 and 4: many ragged sessions at once through cmol_generate_batch
     (one request per session, continuous batching on each GPU).  value =
     generated tokens of all ranks / max over ranks of the device time of all
@@ -109,9 +109,8 @@ def run_batched(args, rank, world, local, barrier):
         launches = st.kernel_launches_per_step
         for s in ss:
             s.release()
-    import torch.distributed as tdist
     (gen_all, prefill_all), (dev_ms, wall_ms, steps) = reduce_ranks(
-        tdist if world > 1 else None, f"cuda:{local}", sums=(gen, int(plen.sum())), maxes=(dev_ms, wall_ms, steps))
+        dist, f"cuda:{local}", sums=(gen, int(plen.sum())), maxes=(dev_ms, wall_ms, steps))
     if rank != 0:
         return
     peak, peak_kind = peaks()
@@ -390,6 +389,8 @@ def run_reference(args, rank, world):
 
 
 def main():
+    import faulthandler
+    faulthandler.enable()          # a native crash prints the Python frames that led to it
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
@@ -431,7 +432,7 @@ def main():
             dist.destroy_process_group()
         return
     if args.workload in ("c3", "c4"):
-        run_batched(args, rank, world, local, barrier)
+        run_batched(args, rank, world, local, barrier, dist)
         if dist is not None:
             dist.destroy_process_group()
         return

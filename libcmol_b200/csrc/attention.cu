@@ -3,6 +3,10 @@
 #include "attention_item.cuh"
 #include "gemv_launch.cuh"
 
+#include <stdlib.h>
+
+#include <algorithm>
+
 size_t attention_smem_bytes(int d_head, int G, int split_tokens) {
     return attn_item_smem_bytes(d_head, G, split_tokens) + 16;   // + the mbarrier
 }
@@ -29,17 +33,103 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a) {
                  sh, threadIdx.x);
 }
 
+// Work-list launch for wide steps: a fixed grid of a few CTAs per SM; each
+// CTA lists the active (column, kv head, split) items of the step from the
+// columns' positions (prefix sum over columns in shared memory) and takes
+// items blockIdx.x, blockIdx.x + gridDim.x, ...  The grid then depends on the
+// SM count, not on the longest context the pool allows, so steps whose
+// sessions are short do not pay for launching (and retiring) the splits they
+// do not have.
+#define ATTN_LIST_MAX_COLS 1024
+// Grids smaller than this launch one CTA per item (measured faster on config 3,
+// ~51K cells: more items in flight than a few CTAs per SM walking a list).
+#define ATTN_LIST_MIN_CELLS 65536
+
 template <int E>
-static cudaError_t launch_e(const AttnArgs &a, dim3 grid, size_t smem, cudaStream_t st, bool pdl) {
+__global__ void __launch_bounds__(ATTN_THREADS) k_attn_list(AttnArgs a, int ncol) {
+    const int G = a.n_heads / a.n_kv;
+    float *sm = reinterpret_cast<float *>(cmolcu_smem);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(cmolcu_smem + attn_item_smem_bytes(32 * E, G, a.split_tokens));
+    __shared__ AttnShared sh;
+    __shared__ int start[ATTN_LIST_MAX_COLS + 1];   // start[c] = first item of column c
+    __shared__ int wsum[ATTN_WARPS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+    // items per column, then an exclusive prefix sum (chunks of ATTN_THREADS columns)
+    const int S = a.split_tokens;
+    int carry = 0;
+    for (int c0 = 0; c0 < ncol; c0 += ATTN_THREADS) {
+        const int c = c0 + tid;
+        int n = 0;
+        if (c < ncol) {
+            const int pos = a.pos[c];
+            n = pos < 0 ? 0 : a.n_kv * (pos / S + 1);
+        }
+        int v = n;   // inclusive scan within the warp
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += t;
+        }
+        if (lane == 31) wsum[warp] = v;
+        named_bar_sync(1, ATTN_THREADS);
+        int before = carry;
+        for (int w = 0; w < warp; w++) before += wsum[w];
+        if (c < ncol) start[c] = before + v - n;
+        int tot = 0;
+        for (int w = 0; w < ATTN_WARPS; w++) tot += wsum[w];
+        carry += tot;
+        named_bar_sync(1, ATTN_THREADS);
+    }
+    if (tid == 0) start[ncol] = carry;
+    named_bar_sync(1, ATTN_THREADS);
+    const int total = carry;
+    uint32_t parity = 0;
+    for (int i = blockIdx.x; i < total; i += gridDim.x) {
+        int lo = 0, hi = ncol - 1;          // last column with start <= i
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (start[mid] <= i) lo = mid; else hi = mid - 1;
+        }
+        const int col = lo, r = i - start[col];
+        const int nsp = (start[col + 1] - start[col]) / a.n_kv;
+        const int hk = r / nsp, sp = r % nsp;
+        const int pos = a.pos[col];
+        const int srow = a.slot ? a.slot[col] : col;
+        if (!attn_item<E>(a, sp, hk, col, pos, a.page_table + (long long)srow * a.max_pages, sm, bar, parity, sh, tid))
+            return;   // fault recorded (uniform over the CTA)
+    }
+}
+
+template <int E>
+static cudaError_t launch_e(const AttnArgs &a, int ncol, size_t smem, cudaStream_t st, bool pdl) {
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {   // per process: the B200s of one box share the limit
         cudaError_t e = cudaFuncSetAttribute(k_attn<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_list<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
-    return launch_k(k_attn<E>, grid, dim3(ATTN_THREADS), smem, st, pdl, a);
+    const long long cells = (long long)a.n_splits * a.n_kv * ncol;
+    const int sms = device_sm_count();
+    const int per_sm = std::max(1, std::min(4, (int)((200 * 1024) / (smem + 8 * 1024))));
+    // CMOLCU_ATTN_LIST=1 / 0: the work-list / grid launch for every step (tests, measurements)
+    static const int mode = [] {
+        const char *v = getenv("CMOLCU_ATTN_LIST");
+        return v && v[0] == '1' ? 1 : v && v[0] == '0' ? 0 : -1;
+    }();
+    const bool list = mode == 1 || (mode < 0 && cells > ATTN_LIST_MIN_CELLS);
+    if (list && ncol <= ATTN_LIST_MAX_COLS)
+        return launch_k(k_attn_list<E>, dim3(sms * per_sm), dim3(ATTN_THREADS), smem, st, pdl, a, ncol);
+    return launch_k(k_attn<E>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
 }
 
 cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl) {
@@ -48,12 +138,11 @@ cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool 
     if (a.split_tokens % a.page_tokens != 0 || a.n_splits < 1) return cudaErrorInvalidValue;
     const size_t smem = attention_smem_bytes(a.d_head, G, a.split_tokens);
     if (smem > CMOLCU_ATTN_SMEM_MAX) return cudaErrorInvalidValue;
-    dim3 grid(a.n_splits, a.n_kv, ncol);
     switch (a.d_head) {
-    case 64:  return launch_e<2>(a, grid, smem, st, pdl);
-    case 128: return launch_e<4>(a, grid, smem, st, pdl);
-    case 32:  return launch_e<1>(a, grid, smem, st, pdl);
-    case 256: return launch_e<8>(a, grid, smem, st, pdl);
+    case 64:  return launch_e<2>(a, ncol, smem, st, pdl);
+    case 128: return launch_e<4>(a, ncol, smem, st, pdl);
+    case 32:  return launch_e<1>(a, ncol, smem, st, pdl);
+    case 256: return launch_e<8>(a, ncol, smem, st, pdl);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -265,33 +265,58 @@ __device__ __forceinline__ void epi_swiglu_pair(const GemvArgs &a, int row, int 
     a.y[(long long)col * a.y_ld + (long long)(row / 2) * a.y_inc] = h;
 }
 
+// Operands the Q/K/V epilogue of rows (lrow, lrow+1) of column col reads
+// from memory: the column's position, the page holding it (k/v rows) and the
+// RoPE (cos, sin) of the pair (q/k rows).  They are fixed for the step, so a
+// kernel can fetch them before its arithmetic.
+struct QkvPre {
+    int    pos, pg;
+    float2 cs;
+};
+
+__device__ __forceinline__ QkvPre epi_qkv_fetch(const GemvArgs &a, int lrow, int col) {
+    const EpiQKV &e = a.qkv;
+    QkvPre q;
+    q.pos = e.pos[col];
+    q.pg = -1;
+    q.cs = make_float2(1.f, 0.f);
+    if (q.pos < 0) return q;
+    const int row = e.row_base + lrow;
+    const int D = e.d_model, KVD = e.kv_dim, hd = e.d_head;
+    if (row >= D) {
+        const int srow = e.slot ? e.slot[col] : col;
+        q.pg = e.page_table[(long long)srow * e.max_pages + q.pos / e.page_tokens];
+    }
+    if (e.rope && row < D + KVD) q.cs = e.rope_cs[(long long)q.pos * (hd / 2) + ((row % hd) >> 1)];
+    return q;
+}
+
 // Fused Q/K/V rows (lrow, lrow+1) of column col (local row numbering; the
 // global row adds qkv.row_base): RoPE on q and k pairs, q to y, k and v into
 // the column's KV page at its position.
-__device__ __forceinline__ void epi_qkv_pair(const GemvArgs &a, int lrow, int col, float v0, float v1) {
+__device__ __forceinline__ void epi_qkv_apply(const GemvArgs &a, int lrow, int col, float v0, float v1,
+                                              const QkvPre &q) {
     const EpiQKV &e = a.qkv;
     const int row = e.row_base + lrow;
-    const int pos = e.pos[col];
+    const int pos = q.pos;
     if (pos < 0) return;
     const int D = e.d_model, KVD = e.kv_dim, hd = e.d_head;
     const bool is_v = row >= D + KVD;
     if (e.rope && !is_v) {
         // NORM-style pair rotation, src/model.c:137-166
-        int i = (row % hd) >> 1;
-        float2 cs = e.rope_cs[(long long)pos * (hd / 2) + i];
+        const float2 cs = q.cs;
         float n0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
         float n1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
         v0 = n0; v1 = n1;
     }
     if (row < D) {
-        float *q = a.y + (long long)col * a.y_ld;
-        q[row] = v0; q[row + 1] = v1;
+        float *qo = a.y + (long long)col * a.y_ld;
+        qo[row] = v0; qo[row + 1] = v1;
         return;
     }
     const int kvr = is_v ? row - D - KVD : row - D;
     const int head = kvr / hd, dim = kvr % hd;
-    const int srow = e.slot ? e.slot[col] : col;
-    const int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
+    const int pg = q.pg;
     if (pg < 0 || pg >= e.n_pages) {   // never write outside the pool
         if (a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
         return;
@@ -302,9 +327,47 @@ __device__ __forceinline__ void epi_qkv_pair(const GemvArgs &a, int lrow, int co
     base[0] = v0; base[1] = v1;
 }
 
+__device__ __forceinline__ void epi_qkv_pair(const GemvArgs &a, int lrow, int col, float v0, float v1) {
+    epi_qkv_apply(a, lrow, col, v0, v1, epi_qkv_fetch(a, lrow, col));
+}
+
+// Epilogue operands prefetched for one warp's first row group: the old
+// residual value (RESID) or the Q/K/V operands (QKV) of the lane's slot.
+struct EpiPre {
+    bool   valid;
+    float  old;
+    QkvPre q;
+};
+
+template <int NC, int R, int EPI>
+__device__ __forceinline__ EpiPre gemv_epi_prefetch(const GemvArgs &a, int row0, int row_end, int lane) {
+    EpiPre pre;
+    pre.valid = false;
+    pre.old = 0.f;
+    pre.q.pos = -1;
+    pre.q.pg = -1;
+    pre.q.cs = make_float2(1.f, 0.f);
+    if (row0 >= row_end) return pre;
+    if constexpr (EPI == EPI_RESID) {
+        if (lane < R * NC) {
+            const int r = lane / NC, col = lane % NC, row = row0 + r;
+            if (row < a.w.rows && col < a.ncol) pre.old = __ldcg(a.y + (long long)col * a.y_ld + (long long)row * a.y_inc);
+        }
+        pre.valid = true;
+    } else if constexpr (EPI == EPI_QKV) {
+        if (lane < (R / 2) * NC) {
+            const int p = lane / NC, col = lane % NC;
+            if (col < a.ncol && row0 + 2 * p + 1 < a.w.rows) pre.q = epi_qkv_fetch(a, row0 + 2 * p, col);
+        }
+        pre.valid = true;
+    }
+    return pre;
+}
+
 // Epilogue; vals[r*NC+col] hold the totals of rows row0..row0+R-1.
 template <int NC, int R, int EPI>
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const float *vals, int lane) {
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const float *vals, int lane,
+                                              const EpiPre *pre = nullptr) {
     const int rows = a.w.rows;
     if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
         if (lane < R * NC) {
@@ -313,7 +376,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const
             if (row < rows && col < a.ncol) {
                 float *p = a.y + (long long)col * a.y_ld + (long long)row * a.y_inc;
                 float v = vals[lane];
-                if constexpr (EPI == EPI_RESID) *p = __ldcg(p) + v;   // x += sublayer out (src/model.c:232,259)
+                if constexpr (EPI == EPI_RESID) *p = (pre && pre->valid ? pre->old : __ldcg(p)) + v;   // x += sublayer out (src/model.c:232,259)
                 else *p = v;
             }
         }
@@ -327,8 +390,12 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, int row0, const
     } else {  // EPI_QKV
         if (lane < (R / 2) * NC) {
             int p = lane / NC, col = lane % NC;
-            if (row0 + 2 * p + 1 < rows && col < a.ncol)
-                epi_qkv_pair(a, row0 + 2 * p, col, vals[(2 * p) * NC + col], vals[(2 * p + 1) * NC + col]);
+            if (row0 + 2 * p + 1 < rows && col < a.ncol) {
+                if (pre && pre->valid)
+                    epi_qkv_apply(a, row0 + 2 * p, col, vals[(2 * p) * NC + col], vals[(2 * p + 1) * NC + col], pre->q);
+                else
+                    epi_qkv_pair(a, row0 + 2 * p, col, vals[(2 * p) * NC + col], vals[(2 * p + 1) * NC + col]);
+            }
         }
     }
 }
@@ -412,6 +479,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(GemvArgs a) {
 
     // ---------------- consumer warps ----------------
     pdl_wait();
+    // the first tile's epilogue operands, in flight while the activations stage
+    const EpiPre pre = gemv_epi_prefetch<NC, R, EPI>(a, row_begin + warp * R, row_end, lane);
     {
         // pass 1: RMS of each column (src/model.c:90-97), when normalising
         if (a.norm_w) {
@@ -513,7 +582,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) k_gemv(GemvArgs a) {
             float vals[R * NC];
 #pragma unroll
             for (int i = 0; i < R * NC; i++) vals[i] = warp_sum(acc[i]) * final_scale<DT>();
-            gemv_epilogue<NC, R, EPI>(a, row0, vals, lane);
+            gemv_epilogue<NC, R, EPI>(a, row0, vals, lane, ti == 0 ? &pre : nullptr);
         }
     }
 }

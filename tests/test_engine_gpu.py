@@ -101,6 +101,34 @@ def test_teacher_forced_logits_tensor_cores(gpu, golden, paths, name, monkeypatc
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q4_k", "smollm3"])
+def test_attention_work_list_launch(gpu, golden, paths, name):
+    """The work-list attention launch (used for wide steps), forced on every
+    step in a fresh process: teacher-forced logits and greedy streams as the
+    grid launch gives them."""
+    import subprocess
+    import sys
+    code = f"""
+import numpy as np, sys
+sys.path.insert(0, {os.path.dirname(GOLD)!r} + "/..")
+from libcmol_b200.model import Model, GenParams
+g = np.load({os.path.join(GOLD, "models.npz")!r})
+with Model({paths[name]!r}, max_ctx=64, max_sessions=2, page_tokens=4) as m:
+    s = m.acquire()
+    for i, t in enumerate(g["{name}_tokens"]):
+        got = s.forward_logits(int(t)); ref = g["{name}_logits"][i]
+        assert float(np.abs(got - ref).max()) < 1e-3, i
+    s.reset()
+    rc, ids = s.generate_ids(g["{name}_tokens"][:6], GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=20))
+    assert rc == 0 and ids == g["{name}_gen_greedy"].tolist(), ids
+print("ok")
+"""
+    env = dict(os.environ, CMOLCU_ATTN_LIST="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
 def test_wide_batch_uses_tensor_cores(gpu, golden, paths):
     """Eight sessions in one step take the tensor-core path (default
     threshold); every session decodes to the requested length, and the
