@@ -369,12 +369,56 @@ def cpu_baseline(args, wl):
                       f"{args.ref_steps} greedy decode steps of the C restatement on {spec.name}"}
 
 
+def reference_gemv_rate(n_threads, reps):
+    """The reference's matmul kernel (cmol_kernels_select().matmul, the
+    AVX-512 path of src/quant.c:488-566) on the config-5 Q4_K weight at n = 1,
+    one weight copy per host thread: aggregate GB/s of GGUF bytes."""
+    import numpy as np
+
+    from libcmol_b200 import synth
+    from oracle.oracle import Reference
+    rng = np.random.default_rng(0)
+    blob = np.ascontiguousarray(synth.quantize(rng.standard_normal((GEMV_M, GEMV_K), dtype=np.float32) * 0.02,
+                                               synth.Q4_K))
+    x = rng.standard_normal(GEMV_K, dtype=np.float32)
+    Reference.matmul(blob, x, GEMV_M, GEMV_K, 1, synth.Q4_K)       # warm-up, kernel selection
+    times = [0.0] * n_threads
+
+    def work(i):
+        b = blob.copy()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            Reference.matmul(b, x, GEMV_M, GEMV_K, 1, synth.Q4_K)
+        times[i] = time.perf_counter() - t0
+
+    th = [threading.Thread(target=work, args=(i,)) for i in range(n_threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    return n_threads * reps * blob.nbytes / max(times) / 1e9, max(times) / reps
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of the path on
     the host cores (see cpu_baseline)."""
     if rank != 0:
         return
     wl = WORKLOADS[args.workload]
+    if args.workload == "c5":
+        cores = os.cpu_count() or 1
+        gbs, sec = reference_gemv_rate(cores, max(4, args.steps // 4))
+        print(json.dumps({
+            "impl": "reference", "metric": "GEMV HBM GB/s (11008x2048 dequant-dot, n=1, Q4_K)", "value": round(gbs, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": max(4, args.steps // 4), "warmup": 1,
+            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": wl["label"]},
+            "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": cores, "kind": "reference",
+                             "sample": f"{cores} host threads, each its own copy of the Q4_K weight, "
+                                       "the reference's selected matmul kernel at n=1"},
+            "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     cb = cpu_baseline(args, wl)
     val = cb["value"]
     print(json.dumps({

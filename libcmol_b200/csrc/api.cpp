@@ -429,7 +429,22 @@ void Worker::run() {
     std::vector<Request *> batch;
     std::vector<int32_t> out;
     const int P = e->page_tokens();
+    // A request belongs to the thread waiting in submit_and_wait, which may
+    // return (and destroy it) as soon as finish() signals it: so a request is
+    // first retired (session pointer cleared, status queued), then removed
+    // from `active`, and only then finished, as the worker's last touch.
+    std::vector<std::pair<Request *, cmol_err_t>> retired;
+    auto retire = [&](Request *r, cmol_err_t st) {
+        r->s = nullptr;
+        retired.emplace_back(r, st);
+    };
     for (;;) {
+        if (!retired.empty()) {
+            active.erase(std::remove_if(active.begin(), active.end(), [](Request *r) { return r->s == nullptr; }),
+                         active.end());
+            for (auto &rs : retired) finish(rs.first, rs.second);
+            retired.clear();
+        }
         {
             std::unique_lock<std::mutex> lk(mu);
             cv.wait(lk, [&] { return stop || !incoming.empty() || !active.empty(); });
@@ -458,7 +473,7 @@ void Worker::run() {
             for (int i = 0; i < seed_n; i++) sp.ring[i] = r->prompt[(size_t)(np - seed_n + i)];
             sp.ring_head = seed_n % kRepeatBuf;
             sp.ring_fill = seed_n;
-            if (e->set_sampler(r->s->slot, sp)) { finish(r, CMOL_ERR_INVALID); r->s = nullptr; }
+            if (e->set_sampler(r->s->slot, sp)) retire(r, CMOL_ERR_INVALID);
         }
         // drop aborted / failed requests
         std::vector<Request *> keep;
@@ -501,7 +516,7 @@ void Worker::run() {
             const int pidx = c.pos / P;
             if (pidx >= (int)s->pages.size()) {
                 std::lock_guard<std::mutex> lk(mu);
-                if (free_pages.empty()) { oom = true; finish(r, CMOL_ERR_OOM); r->s = nullptr; continue; }
+                if (free_pages.empty()) { oom = true; retire(r, CMOL_ERR_OOM); continue; }
                 int pg = free_pages.back();
                 free_pages.pop_back();
                 s->pages.push_back(pg);
@@ -516,7 +531,7 @@ void Worker::run() {
         float *lg = fwd ? fwd->logits_out : nullptr;
         if (e->step(cols, upd, out.data(), lg) != 0) {
             logf(m, CMOL_LOG_ERROR, "decode step failed on GPU %d: %s", e->device(), e->last_error());
-            for (Request *r : batch) { finish(r, CMOL_ERR_INVALID); r->s = nullptr; }
+            for (Request *r : batch) retire(r, CMOL_ERR_INVALID);
             continue;
         }
         // advance every request of the step
@@ -526,7 +541,7 @@ void Worker::run() {
             s->n_tokens = cols[i].pos + 1;
             const int np = (int)r->prompt.size();
             if (r->fed < np) r->fed++;
-            if (r->forward_only) { finish(r, CMOL_OK); r->s = nullptr; continue; }
+            if (r->forward_only) { retire(r, CMOL_OK); continue; }
             if (!cols[i].sample) continue;
             const int32_t t = out[i];
             const int is_eos = (m->eos >= 0 && t == m->eos) ? 1 : 0;
@@ -544,7 +559,7 @@ void Worker::run() {
                 r->q.emplace_back(t, is_eos);
                 r->cv.notify_all();
             }
-            if (done) { finish(r, CMOL_OK); r->s = nullptr; }
+            if (done) retire(r, CMOL_OK);
         }
         keep.clear();
         for (Request *r : active)
