@@ -248,7 +248,10 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
             EngineOptions eo;
             const int per_gpu = (ns + ng - 1) / ng;
             eo.max_slots = ns;
-            eo.max_batch = opt.max_batch > 0 ? std::min(opt.max_batch, per_gpu) : per_gpu;
+            // columns of a step: one per session, plus up to prefill_chunk
+            // (at most 256) further prompt tokens of sessions still in prefill
+            const int prefill = std::max(1, std::min(m->cfg.prefill_chunk, 256));
+            eo.max_batch = (opt.max_batch > 0 ? std::min(opt.max_batch, per_gpu) : per_gpu) + (prefill > 1 ? prefill : 0);
             eo.max_ctx = m->cfg.max_ctx;
             eo.page_tokens = opt.kv_page_tokens > 0 ? opt.kv_page_tokens : 16;
             eo.kv_pool_frac = opt.kv_pool_frac > 0.f ? opt.kv_pool_frac : 0.85f;
@@ -497,18 +500,24 @@ void Worker::run() {
         for (Request *r : active)
             if (r->forward_only) { fwd = r; break; }
         const int cap = e->max_batch();
-        bool oom = false;
-        for (Request *r : active) {
-            if (fwd && r != fwd) continue;
-            if ((int)batch.size() >= cap) break;
+        const int prefill = std::max(1, std::min(m->cfg.prefill_chunk, 256));
+        struct Entry {
+            Request *r;
+            int n;        // columns of this request in the step
+            int scol;     // the column whose sampled token it takes, or -1
+        };
+        std::vector<Entry> ent;
+        // one column of request r at offset `off` past its next token; false
+        // when no KV page is left for it
+        auto add_col = [&](Request *r, int off) -> bool {
             cmol_session_t *s = r->s;
             StepColumn c;
-            c.pos = s->n_tokens;
+            c.pos = s->n_tokens + off;
             c.slot = s->slot;
             const int np = (int)r->prompt.size();
-            if (r->fed < np) {
-                c.token = r->prompt[(size_t)r->fed];
-                c.sample = (!r->forward_only && r->fed == np - 1) ? 1 : 0;
+            if (r->fed + off < np) {
+                c.token = r->prompt[(size_t)(r->fed + off)];
+                c.sample = (!r->forward_only && r->fed + off == np - 1) ? 1 : 0;
             } else {
                 c.token = r->last;
                 c.sample = 1;
@@ -516,16 +525,40 @@ void Worker::run() {
             const int pidx = c.pos / P;
             if (pidx >= (int)s->pages.size()) {
                 std::lock_guard<std::mutex> lk(mu);
-                if (free_pages.empty()) { oom = true; retire(r, CMOL_ERR_OOM); continue; }
+                if (free_pages.empty()) return false;
                 int pg = free_pages.back();
                 free_pages.pop_back();
                 s->pages.push_back(pg);
                 upd.push_back(PageUpdate{s->slot, pidx, pg});
             }
             cols.push_back(c);
+            return true;
+        };
+        // pass 1: the next token of every request (decode or prompt)
+        for (Request *r : active) {
+            if (fwd && r != fwd) continue;
+            if ((int)cols.size() >= cap) break;
+            if (!add_col(r, 0)) { retire(r, CMOL_ERR_OOM); continue; }
+            ent.push_back(Entry{r, 1, cols.back().sample ? (int)cols.size() - 1 : -1});
             batch.push_back(r);
         }
-        (void)oom;
+        // pass 2: batched prefill, further prompt tokens of the same sessions as
+        // columns at consecutive positions (each step's Q/K/V kernel writes all
+        // columns' keys and values before attention reads them, so a column
+        // attends to the prompt tokens before it in the same step)
+        if (!fwd && prefill > 1) {
+            for (Entry &en : ent) {
+                Request *r = en.r;
+                const int np = (int)r->prompt.size();
+                bool full = false;
+                while (en.n < prefill && r->fed + en.n < np && (int)cols.size() < cap) {
+                    if (!add_col(r, en.n)) { full = true; break; }
+                    if (cols.back().sample) en.scol = (int)cols.size() - 1;
+                    en.n++;
+                }
+                if (full || (int)cols.size() >= cap) break;
+            }
+        }
         if (batch.empty()) continue;
         out.assign(cols.size(), -1);
         float *lg = fwd ? fwd->logits_out : nullptr;
@@ -535,15 +568,15 @@ void Worker::run() {
             continue;
         }
         // advance every request of the step
-        for (size_t i = 0; i < batch.size(); i++) {
-            Request *r = batch[i];
+        for (const Entry &en : ent) {
+            Request *r = en.r;
             cmol_session_t *s = r->s;
-            s->n_tokens = cols[i].pos + 1;
+            s->n_tokens += en.n;
             const int np = (int)r->prompt.size();
-            if (r->fed < np) r->fed++;
+            if (r->fed < np) r->fed += en.n;
             if (r->forward_only) { retire(r, CMOL_OK); continue; }
-            if (!cols[i].sample) continue;
-            const int32_t t = out[i];
+            if (en.scol < 0) continue;
+            const int32_t t = out[(size_t)en.scol];
             const int is_eos = (m->eos >= 0 && t == m->eos) ? 1 : 0;
             bool done = false;
             if (is_eos) {

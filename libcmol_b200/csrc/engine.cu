@@ -72,7 +72,7 @@ struct Engine::Impl {
     // tensor-core matmul for steps of >= tc_min_cols columns (gemm_tc.cuh)
     TcScratch     tc = {};
     bool          tc_ok = false;
-    int           tc_min_cols = 8;
+    int           tc_min_cols = 16;
     // CMOLCU_DS_TRACE=1: per-phase timing of CTA 0, summed over steps, printed at exit
     unsigned long long *ds_trace = nullptr;
     std::vector<unsigned long long> ds_trace_host;
@@ -264,7 +264,7 @@ static void build_tensor_core_path(Engine *e, Engine::Impl *d, EngineBuilder &b)
         if (!w.base || !tc_supported(w.q.dtype)) return;
         size_t a = 0, p = 0;
         int r = 0;
-        tc_scratch_need(w.q.rows, w.q.k, o.max_batch, &a, &p, &r);
+        tc_scratch_need(w.q.rows, w.q.k, std::min(o.max_batch, TC_MAX_N), &a, &p, &r);
         xs = std::max(xs, a);
         part = std::max(part, p);
         rbs = std::max(rbs, r);
@@ -522,8 +522,22 @@ int Engine::set_sampler(int slot, const SamplerParams &p) {
 static cudaError_t step_matmul(Engine::Impl *d, const GemvArgs &a, int ncol, int epi, cudaStream_t st, bool pdl,
                                int &launches) {
     if (d->tc_ok && ncol >= d->tc_min_cols && tc_supported(a.w.dtype) && a.w.k % TC_KB == 0 && a.w.kc % TC_KB == 0) {
-        launches += 2;
-        return tc_matmul(a, ncol, epi, d->tc, st, pdl);
+        // blocks of at most TC_MAX_N columns (one tensor-memory accumulator each)
+        for (int c0 = 0; c0 < ncol; c0 += TC_MAX_N) {
+            GemvArgs b = a;
+            const int n = std::min(TC_MAX_N, ncol - c0);
+            b.x = a.x + (long long)c0 * a.x_ld;
+            b.y = a.y + (long long)c0 * a.y_ld;
+            if (epi == EPI_QKV) {
+                b.qkv.pos = a.qkv.pos + c0;
+                if (a.qkv.slot) b.qkv.slot = a.qkv.slot + c0;
+                else b.qkv.page_table = a.qkv.page_table + (long long)c0 * a.qkv.max_pages;
+            }
+            launches += 2;
+            cudaError_t e = tc_matmul(b, n, epi, d->tc, st, pdl);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
     }
     launches += (ncol + 1) / 2;
     return gemv_launch_cols(a, ncol, epi, st, pdl);

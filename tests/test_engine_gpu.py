@@ -130,20 +130,20 @@ print("ok")
 
 @pytest.mark.gpu
 def test_wide_batch_uses_tensor_cores(gpu, golden, paths):
-    """Eight sessions in one step take the tensor-core path (default
+    """Sixteen sessions in one step take the tensor-core path (default
     threshold); every session decodes to the requested length, and the
     greedy streams agree with the reference up to f16 rounding (reported)."""
     from libcmol_b200.model import GenParams, Model
     name = "q4_k"
-    with Model(paths[name], max_ctx=64, max_sessions=8) as m:
-        ss = [m.acquire() for _ in range(8)]
+    with Model(paths[name], max_ctx=64, max_sessions=16) as m:
+        ss = [m.acquire() for _ in range(16)]
         prompt = golden[f"{name}_tokens"][:6]
         p = GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=20)
-        outs = m.generate_batch(ss, [prompt] * 8, [p] * 8)
+        outs = m.generate_batch(ss, [prompt] * 16, [p] * 16)
         ref = golden[f"{name}_gen_greedy"].tolist()
         assert all(len(o) == len(ref) for o in outs)
         same = sum(o.tolist() == ref for o in outs)
-        print(f"wide batch: {same}/8 streams identical to the reference")
+        print(f"wide batch: {same}/16 streams identical to the reference")
         assert all(o[0] == ref[0] for o in outs)
         st = m.stats(0)
         assert st.kernel_launches_per_step > 0
