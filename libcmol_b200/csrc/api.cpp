@@ -252,6 +252,7 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
             // (at most 256) further prompt tokens of sessions still in prefill
             const int prefill = std::max(1, std::min(m->cfg.prefill_chunk, 256));
             eo.max_batch = (opt.max_batch > 0 ? std::min(opt.max_batch, per_gpu) : per_gpu) + (prefill > 1 ? prefill : 0);
+            eo.max_group = prefill;
             eo.max_ctx = m->cfg.max_ctx;
             eo.page_tokens = opt.kv_page_tokens > 0 ? opt.kv_page_tokens : 16;
             eo.kv_pool_frac = opt.kv_pool_frac > 0.f ? opt.kv_pool_frac : 0.85f;
@@ -534,30 +535,44 @@ void Worker::run() {
             cols.push_back(c);
             return true;
         };
-        // pass 1: the next token of every request (decode or prompt)
-        for (Request *r : active) {
-            if (fwd && r != fwd) continue;
-            if ((int)cols.size() >= cap) break;
-            if (!add_col(r, 0)) { retire(r, CMOL_ERR_OOM); continue; }
-            ent.push_back(Entry{r, 1, cols.back().sample ? (int)cols.size() - 1 : -1});
-            batch.push_back(r);
-        }
+        // pass 1: the next token of every request (decode or prompt);
         // pass 2: batched prefill, further prompt tokens of the same sessions as
         // columns at consecutive positions (each step's Q/K/V kernel writes all
         // columns' keys and values before attention reads them, so a column
-        // attends to the prompt tokens before it in the same step)
+        // attends to the prompt tokens before it in the same step).  A session's
+        // columns are emitted together, in increasing position: attention serves
+        // such a group from one load of its keys and values.
+        std::vector<int> want;
+        std::vector<Request *> order;
+        int ncols = 0;
+        for (Request *r : active) {
+            if (fwd && r != fwd) continue;
+            if (ncols >= cap) break;
+            order.push_back(r);
+            want.push_back(1);
+            ncols++;
+        }
         if (!fwd && prefill > 1) {
-            for (Entry &en : ent) {
-                Request *r = en.r;
+            for (size_t i = 0; i < order.size() && ncols < cap; i++) {
+                Request *r = order[i];
                 const int np = (int)r->prompt.size();
-                bool full = false;
-                while (en.n < prefill && r->fed + en.n < np && (int)cols.size() < cap) {
-                    if (!add_col(r, en.n)) { full = true; break; }
-                    if (cols.back().sample) en.scol = (int)cols.size() - 1;
-                    en.n++;
+                while (want[i] < prefill && r->fed + want[i] < np && ncols < cap) {
+                    want[i]++;
+                    ncols++;
                 }
-                if (full || (int)cols.size() >= cap) break;
             }
+        }
+        for (size_t i = 0; i < order.size(); i++) {
+            Request *r = order[i];
+            Entry en{r, 0, -1};
+            for (int k = 0; k < want[i]; k++) {
+                if (!add_col(r, k)) break;          // no KV page left: take fewer tokens
+                if (cols.back().sample) en.scol = (int)cols.size() - 1;
+                en.n++;
+            }
+            if (en.n == 0) { retire(r, CMOL_ERR_OOM); continue; }
+            ent.push_back(en);
+            batch.push_back(r);
         }
         if (batch.empty()) continue;
         out.assign(cols.size(), -1);

@@ -7,11 +7,19 @@
 
 #include <algorithm>
 
-size_t attention_smem_bytes(int d_head, int G, int split_tokens) {
-    return attn_item_smem_bytes(d_head, G, split_tokens) + 16;   // + the mbarrier
+size_t attention_smem_bytes(int d_head, int G, int split_tokens, int q_chunk) {
+    return attn_group_smem_bytes(d_head, G, split_tokens, q_chunk) + 16;   // + the mbarrier
 }
 
-// One CTA per item: grid (split, kv head, column).
+int attention_q_chunk(int d_head, int G, int split_tokens) {
+    // 6 KB: configs 1-4 keep the CTAs per SM of the one-query layout, but for
+    // SmolLM2-1.7B's (G = 1), which goes from 6 to 5
+    return attn_group_qc(d_head, G, split_tokens, 6 * 1024);
+}
+
+
+// Steps without prefill groups: one CTA per (split, kv head, column), each
+// running attn_item.
 template <int E>
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a) {
     const int G = a.n_heads / a.n_kv;
@@ -31,6 +39,45 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a) {
     const int srow = a.slot ? a.slot[col] : col;
     attn_item<E>(a, blockIdx.x, blockIdx.y, col, pos, a.page_table + (long long)srow * a.max_pages, sm, bar, parity,
                  sh, threadIdx.x);
+}
+
+// Steps with prefill groups: one CTA per (split, kv head, column).  A column
+// alone in its session (decode) runs attn_item; the columns of a prefill
+// group are served by their block leaders (attn_group_item).  CTAs per SM
+// that the shared memory of the engine's shapes allows (d_head 64: 5, 128:
+// 3); registers are held to that.
+template <int E>
+__global__ void __launch_bounds__(ATTN_THREADS, E <= 2 ? 5 : E == 4 ? 3 : 2) k_attn_group(AttnArgs a) {
+    const int G = a.n_heads / a.n_kv;
+    float *sm = reinterpret_cast<float *>(cmolcu_smem);
+    uint64_t *bar =
+        reinterpret_cast<uint64_t *>(cmolcu_smem + attn_group_smem_bytes(32 * E, G, a.split_tokens, a.q_chunk));
+    __shared__ union {
+        AttnShared      one;
+        AttnGroupShared grp;
+    } sh;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+    named_bar_sync(1, ATTN_THREADS);
+    uint32_t parity = 0;
+    const int c = blockIdx.z, ncol = gridDim.z;
+    // the column and its neighbours, loaded together
+    const int cp = c > 0 ? c - 1 : c, cn = c + 1 < ncol ? c + 1 : c;
+    const int pos = a.pos[c], pos_p = a.pos[cp], pos_n = a.pos[cn];
+    int slot = c, slot_p = cp, slot_n = cn;
+    if (a.slot) { slot = a.slot[c]; slot_p = a.slot[cp]; slot_n = a.slot[cn]; }
+    const bool grouped = a.slot && a.grouped;
+    const bool prev = grouped && cp != c && slot_p == slot && pos_p == pos - 1;
+    const bool next = grouped && cn != c && slot_n == slot && pos_n == pos + 1;
+    if (pos >= 0 && (prev || next))
+        attn_group_item<E>(a, blockIdx.x, blockIdx.y, c, pos, slot, next, sm, bar, parity, sh.grp, threadIdx.x);
+    else
+        attn_item<E>(a, blockIdx.x, blockIdx.y, c, pos, a.page_table + (long long)slot * a.max_pages, sm, bar, parity,
+                     sh.one, threadIdx.x);
 }
 
 // Work-list launch (opt-in): a fixed grid of a few CTAs per SM; each
@@ -111,11 +158,12 @@ static cudaError_t launch_e(const AttnArgs &a, int ncol, size_t smem, cudaStream
     if (attr_dev != dev) {   // per process: the B200s of one box share the limit
         cudaError_t e = cudaFuncSetAttribute(k_attn<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
         if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_attn_group<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
+        if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_attn_list<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
-    const long long cells = (long long)a.n_splits * a.n_kv * ncol;
     const int sms = device_sm_count();
     const int per_sm = std::max(1, std::min(4, (int)((200 * 1024) / (smem + 8 * 1024))));
     // The grid launch (one CTA per item, inactive splits exit at once) measured
@@ -127,10 +175,11 @@ static cudaError_t launch_e(const AttnArgs &a, int ncol, size_t smem, cudaStream
         const char *v = getenv("CMOLCU_ATTN_LIST");
         return v && v[0] == '1';
     }();
-    (void)cells;
     const bool list = force_list;
-    if (list && ncol <= ATTN_LIST_MAX_COLS)
+    if (list && ncol <= ATTN_LIST_MAX_COLS)   // per-column items (no prefill groups)
         return launch_k(k_attn_list<E>, dim3(sms * per_sm), dim3(ATTN_THREADS), smem, st, pdl, a, ncol);
+    if (a.grouped)
+        return launch_k(k_attn_group<E>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
     return launch_k(k_attn<E>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
 }
 
@@ -138,8 +187,11 @@ cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool 
     const int G = a.n_heads / a.n_kv;
     if (a.n_heads % a.n_kv != 0 || G > ATTN_MAX_G) return cudaErrorInvalidValue;
     if (a.split_tokens % a.page_tokens != 0 || a.n_splits < 1) return cudaErrorInvalidValue;
-    const size_t smem = attention_smem_bytes(a.d_head, G, a.split_tokens);
-    if (smem > CMOLCU_ATTN_SMEM_MAX) return cudaErrorInvalidValue;
+    if (a.q_chunk < 1 || a.q_chunk > ATTN_QB || a.q_block < 1 || a.q_block > ATTN_QB) return cudaErrorInvalidValue;
+    // the group layout (a superset of the one-query layout) bounds both kernels
+    if (attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk) > CMOLCU_ATTN_SMEM_MAX) return cudaErrorInvalidValue;
+    const size_t smem = a.grouped ? attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk)
+                                  : attn_item_smem_bytes(a.d_head, G, a.split_tokens) + 16;
     switch (a.d_head) {
     case 64:  return launch_e<2>(a, ncol, smem, st, pdl);
     case 128: return launch_e<4>(a, ncol, smem, st, pdl);

@@ -29,6 +29,9 @@ struct AttnArgs {
     int          layer, n_heads, n_kv, d_head, page_tokens;
     int          split_tokens;   // multiple of page_tokens
     int          n_splits;       // gridDim.x
+    int          q_chunk;        // queries per shared-memory chunk of a prefill group (>= 1)
+    int          grouped;        // 1: a session's consecutive columns share K / V loads
+    int          q_block;        // queries per leader of a group (1..32)
     float        scale;          // 1/sqrt(d_head)
     float       *part;           // scratch [ncol][n_heads][n_splits][d_head + 2]
     int         *counters;       // scratch [ncol][n_kv], zero between launches
@@ -39,8 +42,12 @@ inline size_t attn_part_floats(int ncol, int n_heads, int n_splits, int d_head) 
     return (size_t)ncol * n_heads * n_splits * (d_head + 2);
 }
 
-// Dynamic shared memory one CTA needs (K and V tiles, queries, scores).
-size_t attention_smem_bytes(int d_head, int group, int split_tokens);
+// Dynamic shared memory one CTA needs (K and V tiles, queries, scores) with
+// q_chunk queries per chunk.
+size_t attention_smem_bytes(int d_head, int group, int split_tokens, int q_chunk);
+// Queries per chunk for engines whose steps carry prefill groups: about 6 KB
+// of query and score tiles (decode-only engines use 1).
+int attention_q_chunk(int d_head, int group, int split_tokens);
 #define CMOLCU_ATTN_SMEM_MAX (200 * 1024)
 
 cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl);

@@ -138,10 +138,32 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
     // P.V: item = (head, float4 of d_head); the split's tokens are divided
     // among `parts` thread groups whose float4 sums meet in shared memory.
     {
-        const int items = G * HD4;
+        const int items = G * HD4;   // up to 2 * ATTN_THREADS (G = 8, d_head = 256)
         const int parts = max(1, min(ATTN_THREADS / items, n));
         const int item = tid % items, part = tid / items;
-        if (part < parts) {
+        if (items > ATTN_THREADS) {
+            // one thread per item over all tokens, two items per thread
+            for (int it = tid; it < items; it += ATTN_THREADS) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                const int g = it / HD4, c = it % HD4;
+                const float *p = Sc + g * S;
+                const float4 *V4 = reinterpret_cast<const float4 *>(Vs) + c;
+                for (int t = 0; t < n; t++) {
+                    const float pt_ = p[t];
+                    const float4 v = V4[(size_t)t * HD4];
+                    acc.x = __fmaf_rn(pt_, v.x, acc.x);
+                    acc.y = __fmaf_rn(pt_, v.y, acc.y);
+                    acc.z = __fmaf_rn(pt_, v.z, acc.z);
+                    acc.w = __fmaf_rn(pt_, v.w, acc.w);
+                }
+                float *pp = a.part + (((long long)col * a.n_heads + hk * G + g) * a.n_splits + s) * (hd + 2);
+                pp[4 * c + 0] = acc.x;
+                pp[4 * c + 1] = acc.y;
+                pp[4 * c + 2] = acc.z;
+                pp[4 * c + 3] = acc.w;
+                if (c == 0) { pp[hd] = sh.wmax[g]; pp[hd + 1] = sh.wsum[g]; }
+            }
+        } else if (part < parts) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             const int g = item / HD4, c = item % HD4;
             const float *p = Sc + g * S;
@@ -158,7 +180,7 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
             Red[tid] = acc;
         }
         named_bar_sync(1, ATTN_THREADS);
-        for (int i = tid; i < items; i += ATTN_THREADS) {
+        for (int i = tid; i < items && items <= ATTN_THREADS; i += ATTN_THREADS) {
             float4 r = Red[i];
             for (int q = 1; q < parts; q++) {
                 const float4 o = Red[q * items + i];
@@ -201,5 +223,251 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
     if (tid == 0) a.counters[col * a.n_kv + hk] = 0;
     // the Red / Sc buffers are reused by the next item
     named_bar_sync(1, ATTN_THREADS);
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// Group-aware item.  The columns of one session in a step (same page-table
+// row, contiguous, consecutive positions: a prefill chunk) form a group.  The
+// group's columns at positions p with (p + 1) % a.q_block == 0, and its last
+// column, are leaders: the CTA of a leader serves the up to a.q_block
+// queries of the group ending at it from one
+// load of the split's keys and values; the other columns' CTAs return at
+// once.  Each query attends causally to the split's tokens up to its own
+// position.  Queries go through in chunks of `a.q_chunk` (Q and score tiles
+// in shared memory).  Every query with tokens in the split writes its
+// partial, and the item that completes a query's split count merges it, in
+// split order.
+// ---------------------------------------------------------------------------
+#define ATTN_QB 32   // most queries of one leader (a warp's lanes scan them)
+
+// Query-chunk size for a budget of `budget` bytes of query and score tiles.
+__host__ __device__ inline int attn_group_qc(int d_head, int G, int split_tokens, int budget) {
+    const int per_q = G * (d_head + split_tokens) * 4;
+    const int qc = budget / per_q;
+    return qc < 1 ? 1 : qc > ATTN_QB ? ATTN_QB : qc;
+}
+
+// K and V tiles, query and score tiles, P.V sums, per-row max / sum and
+// per-query merge flags (floats, 16-byte multiple).
+__host__ __device__ inline size_t attn_group_smem_bytes(int d_head, int G, int split_tokens, int qc) {
+    const size_t tail = ((size_t)2 * qc * G * 4 + (size_t)qc * 4 + 15) & ~(size_t)15;
+    return (size_t)2 * split_tokens * d_head * 4 + (size_t)qc * G * d_head * 4 + (size_t)qc * G * split_tokens * 4 +
+           (size_t)ATTN_THREADS * 16 + tail;
+}
+
+struct AttnGroupShared {
+    int q_lo, ok;
+};
+
+// Column c (position pos_c >= 0, page-table row slot_c) belongs to a group
+// of more than one column; `next` says whether column c + 1 continues it.
+// a.slot is non-null.
+template <int E>
+__device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos_c, int slot_c, bool next, float *sm,
+                                uint64_t *bar, uint32_t &parity, AttnGroupShared &gs, int tid) {
+    constexpr int hd = 32 * E, HD4 = hd / 4;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int G = a.n_heads / a.n_kv;
+    const int S = a.split_tokens;
+    const int P = a.page_tokens;
+    const int QC = a.q_chunk;
+    const int QB = a.q_block;
+
+    // a column whose successor continues its group leads only at a block end
+    if (next && (pos_c + 1) % QB != 0) return true;
+    const int t0 = s * S;
+    if (t0 > pos_c) return true;
+    const int n = min(S, pos_c + 1 - t0);                     // tokens of this split the block sees
+
+    float *Ks = sm;                                           // [S][hd]
+    float *Vs = Ks + (size_t)S * hd;                          // [S][hd]
+    float *Qs = Vs + (size_t)S * hd;                          // [QC][G][hd]
+    float *Sc = Qs + (size_t)QC * G * hd;                     // [QC][G][S]
+    float4 *Red = reinterpret_cast<float4 *>(Sc + (size_t)QC * G * S);   // [ATTN_THREADS]
+    float *Wmax = reinterpret_cast<float *>(Red + ATTN_THREADS);         // [QC][G]
+    float *Wsum = Wmax + QC * G;                                          // [QC][G]
+    int *Merge = reinterpret_cast<int *>(Wsum + QC * G);                  // [QC]
+    const int *pt = a.page_table + (long long)slot_c * a.max_pages;
+    const long long head_off = ((long long)a.layer * 2 * a.n_kv + hk) * P * hd;
+    const long long v_off = (long long)a.n_kv * P * hd;
+
+    if (tid == 0) {
+        int ok = 1;
+        const int npg = (n + P - 1) / P;
+        for (int i = 0; i < npg; i++) {
+            int pg = pt[t0 / P + i];
+            if (pg < 0 || pg >= a.n_pages) ok = 0;
+        }
+        if (ok) {
+            fence_proxy_async_global();   // the KV rows of this step were written through the generic proxy
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * npg * P * hd * 4));
+            for (int i = 0; i < npg; i++) {
+                const float *kp = a.kv_pages + (long long)pt[t0 / P + i] * a.page_floats + head_off;
+                bulk_g2s(Ks + (size_t)i * P * hd, kp, (uint32_t)(P * hd * 4), bar);
+                bulk_g2s(Vs + (size_t)i * P * hd, kp + v_off, (uint32_t)(P * hd * 4), bar);
+            }
+        } else if (a.fault) {
+            atomicExch(a.fault, FAULT_BAD_PAGE);
+        }
+        gs.ok = ok;
+    }
+    if (warp == 0) {
+        // the block's first query: lane k (1 <= k <= pos_c % ATTN_QB) checks
+        // that column c - k continues the group; the block starts after the
+        // nearest break
+        const int back = pos_c % QB;
+        const int q = c - lane;
+        const bool brk = lane >= 1 && lane <= back && (q < 0 || a.slot[q] != slot_c || a.pos[q] != pos_c - lane);
+        const unsigned m = __ballot_sync(0xffffffffu, brk);
+        if (lane == 0) gs.q_lo = m ? c - (__ffs(m) - 1) + 1 : c - back;
+    }
+    named_bar_sync(1, ATTN_THREADS);
+    if (!gs.ok) return false;
+    // queries before c - (pos_c - t0) do not reach this split
+    const int q_first = max(gs.q_lo, c - (pos_c - t0));
+    auto load_q = [&](int qb) {
+        const int rows = min(QC, c + 1 - qb) * G;
+        for (int i = tid; i < rows * hd; i += ATTN_THREADS) {
+            const int qi = i / (G * hd), rem = i % (G * hd);
+            Qs[i] = __ldcg(a.q + (long long)(qb + qi) * a.q_ld + (long long)hk * G * hd + rem);
+        }
+    };
+    load_q(q_first);                        // in flight with the K / V copies
+    const bool got = mbar_wait(bar, parity, a.fault, FAULT_ATTN_WAIT);
+    parity ^= 1u;
+    if (!got) gs.ok = 0;
+    named_bar_sync(1, ATTN_THREADS);
+    if (!gs.ok) return false;
+
+    for (int qb = q_first; qb <= c; qb += QC) {
+        const int qn = min(QC, c + 1 - qb);
+        const int rows = qn * G;
+        if (qb != q_first) {
+            load_q(qb);
+            named_bar_sync(1, ATTN_THREADS);
+        }
+        // scores: one thread per (query, head, token); tokens past a query's
+        // position are masked.  Lane l starts its walk over the row at float4
+        // l % HD4 (distinct bank groups across the lanes of a phase).
+        {
+            const float4 *K4 = reinterpret_cast<const float4 *>(Ks);
+            const float4 *Q4 = reinterpret_cast<const float4 *>(Qs);
+            for (int w = tid; w < rows * n; w += ATTN_THREADS) {
+                const int t = w % n, row = w / n, qi = row / G;
+                const int nq = min(n, pos_c - (c - (qb + qi)) + 1 - t0);   // consecutive positions
+                float sc = -INFINITY;
+                if (t < nq) {
+                    const float4 *kr = K4 + (size_t)t * HD4;
+                    const float4 *qr = Q4 + (size_t)row * HD4;
+                    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+                    for (int j = 0; j < HD4; j++) {
+                        const int cc = (j + lane) & (HD4 - 1);
+                        const float4 k = kr[cc], q = qr[cc];
+                        d0 = __fmaf_rn(q.x, k.x, d0);
+                        d1 = __fmaf_rn(q.y, k.y, d1);
+                        d0 = __fmaf_rn(q.z, k.z, d0);
+                        d1 = __fmaf_rn(q.w, k.w, d1);
+                    }
+                    sc = (d0 + d1) * a.scale;
+                }
+                Sc[row * S + t] = sc;
+            }
+        }
+        named_bar_sync(1, ATTN_THREADS);
+        // softmax of each (query, head) row over its visible tokens
+        for (int row = warp; row < rows; row += ATTN_WARPS) {
+            float m = -INFINITY;
+            for (int t = lane; t < n; t += 32) m = fmaxf(m, Sc[row * S + t]);
+            m = warp_max(m);
+            float sum = 0.f;
+            for (int t = lane; t < n; t += 32) {
+                const float v = Sc[row * S + t];
+                const float e = v == -INFINITY ? 0.f : expf(v - m);
+                Sc[row * S + t] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) { Wmax[row] = m; Wsum[row] = sum; }
+        }
+        named_bar_sync(1, ATTN_THREADS);
+        // P.V: item = (row, float4 of d_head).  Few items: the tokens are
+        // divided among `parts` thread groups whose sums meet in shared memory;
+        // many: one thread per item over all tokens.
+        {
+            const int items = rows * HD4;
+            const int parts = items * 2 <= ATTN_THREADS ? max(1, min(ATTN_THREADS / items, n)) : 1;
+            auto write = [&](int it, float4 r) {
+                const int row = it / HD4, cc = it % HD4, qi = row / G, g = row % G;
+                float *pp = a.part + (((long long)(qb + qi) * a.n_heads + hk * G + g) * a.n_splits + s) * (hd + 2);
+                pp[4 * cc + 0] = r.x; pp[4 * cc + 1] = r.y; pp[4 * cc + 2] = r.z; pp[4 * cc + 3] = r.w;
+                if (cc == 0) { pp[hd] = Wmax[row]; pp[hd + 1] = Wsum[row]; }
+            };
+            auto pv = [&](int it, int tb, int te) {
+                const int row = it / HD4, cc = it % HD4;
+                const float *p = Sc + row * S;
+                const float4 *V4 = reinterpret_cast<const float4 *>(Vs) + cc;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int t = tb; t < te; t++) {
+                    const float pt_ = p[t];
+                    const float4 v = V4[(size_t)t * HD4];
+                    acc.x = __fmaf_rn(pt_, v.x, acc.x);
+                    acc.y = __fmaf_rn(pt_, v.y, acc.y);
+                    acc.z = __fmaf_rn(pt_, v.z, acc.z);
+                    acc.w = __fmaf_rn(pt_, v.w, acc.w);
+                }
+                return acc;
+            };
+            if (parts > 1) {
+                const int item = tid % items, part = tid / items;
+                if (part < parts)
+                    Red[tid] = pv(item, (int)((long long)n * part / parts), (int)((long long)n * (part + 1) / parts));
+                named_bar_sync(1, ATTN_THREADS);
+                for (int i = tid; i < items; i += ATTN_THREADS) {
+                    float4 r = Red[i];
+                    for (int q = 1; q < parts; q++) {
+                        const float4 o = Red[q * items + i];
+                        r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
+                    }
+                    write(i, r);
+                }
+            } else {
+                for (int it = tid; it < items; it += ATTN_THREADS) write(it, pv(it, 0, n));
+            }
+        }
+        __threadfence();
+        named_bar_sync(1, ATTN_THREADS);
+        // count this split for each query of the chunk; merge the ones it completes
+        if (tid < qn) {
+            const int q = qb + tid;
+            const int n_active = (pos_c - (c - q) + S) / S;
+            const int old = atomicAdd(&a.counters[q * a.n_kv + hk], 1);
+            Merge[tid] = (old == n_active - 1);
+        }
+        named_bar_sync(1, ATTN_THREADS);
+        __threadfence();
+        for (int qi = 0; qi < qn; qi++) {
+            if (!Merge[qi]) continue;      // uniform: shared flag
+            const int q = qb + qi;
+            const int n_active = (pos_c - (c - q) + S) / S;
+            for (int i = tid; i < G * hd; i += ATTN_THREADS) {
+                const int g = i / hd, d = i % hd;
+                const float *base = a.part + ((long long)q * a.n_heads + hk * G + g) * a.n_splits * (hd + 2);
+                float M = -INFINITY;
+                for (int sp = 0; sp < n_active; sp++) M = fmaxf(M, __ldcg(base + sp * (hd + 2) + hd));
+                float L = 0.f, A = 0.f;
+                for (int sp = 0; sp < n_active; sp++) {
+                    const float *pp = base + sp * (hd + 2);
+                    const float f = expf(__ldcg(pp + hd) - M);
+                    L = __fmaf_rn(__ldcg(pp + hd + 1), f, L);
+                    A = __fmaf_rn(__ldcg(pp + d), f, A);
+                }
+                a.out[(long long)q * a.out_ld + (long long)(hk * G + g) * hd + d] = A / L;
+            }
+            if (tid == 0) a.counters[q * a.n_kv + hk] = 0;
+        }
+        named_bar_sync(1, ATTN_THREADS);     // the tiles are reused by the next chunk
+    }
     return true;
 }

@@ -57,6 +57,9 @@ struct Engine::Impl {
     int   *counters = nullptr;
     unsigned int *fault = nullptr;
     int    n_splits = 1;
+    int    attn_qc = 1;        // attention queries per chunk of a prefill group
+    int    attn_grouped = 1;   // CMOLCU_ATTN_GROUP=0: every column loads its own K / V
+    int    attn_qb = 8;        // queries per group leader (CMOLCU_ATTN_QB; 8 measured best)
     long long n_pages = 0;
     cudaStream_t stream = nullptr;
     cudaEvent_t  ev0 = nullptr, ev1 = nullptr;
@@ -305,13 +308,18 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     e->opt_ = o;
     // attention keeps a whole split of K and V in shared memory: shrink the
     // split (in whole pages) until it fits
+    auto q_chunk = [&](int split) { return o.max_group > 1 ? attention_q_chunk(hd, hp.n_heads / nkv, split) : 1; };
     while (e->opt_.split_tokens > o.page_tokens &&
-           attention_smem_bytes(hd, hp.n_heads / nkv, e->opt_.split_tokens) > CMOLCU_ATTN_SMEM_MAX)
+           attention_smem_bytes(hd, hp.n_heads / nkv, e->opt_.split_tokens, q_chunk(e->opt_.split_tokens)) >
+               CMOLCU_ATTN_SMEM_MAX)
         e->opt_.split_tokens -= o.page_tokens;
     e->vocab_ = V;
     Impl *d = new Impl();
     e->d = d;
     d->hp = hp;
+    d->attn_qc = q_chunk(e->opt_.split_tokens);
+    if (const char *v = getenv("CMOLCU_ATTN_GROUP")) d->attn_grouped = v[0] != '0';
+    if (const char *v = getenv("CMOLCU_ATTN_QB")) d->attn_qb = std::max(1, std::min(32, atoi(v)));
     EngineBuilder b{e, d, msg, msg_len};
     auto fail = [&](int code) -> Engine * { *err = code; delete e; return nullptr; };
 
@@ -545,7 +553,7 @@ static cudaError_t step_matmul(Engine::Impl *d, const GemvArgs &a, int ncol, int
 
 // Records the kernels of one step for `ncol` columns on the engine stream.
 static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol, int max_pages, int &launches,
-                               bool gemv_only = false) {
+                               bool gemv_only = false, bool grouped = false) {
     const HParams &hp = d->hp;
     const int D = hp.d_model, F = hp.d_ffn, V = hp.vocab_size;
     const int hd = hp.d_head, nkv = hp.n_kv_heads, KVD = nkv * hd;
@@ -582,7 +590,8 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         at.kv_pages = d->kv_pages; at.page_floats = d->page_floats; at.n_pages = (int)d->n_pages;
         at.fault = d->fault;
         at.layer = 0; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;
-        at.split_tokens = o.split_tokens; at.n_splits = d->n_splits;
+        at.split_tokens = o.split_tokens; at.n_splits = d->n_splits; at.q_chunk = d->attn_qc; at.grouped = grouped;
+        at.q_block = d->attn_qb;
         at.scale = 1.0f / sqrtf((float)hd);
         at.part = d->part; at.counters = d->counters;
         da.sync_count = d->ds_sync;
@@ -660,7 +669,8 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         at.kv_pages = d->kv_pages; at.page_floats = d->page_floats; at.n_pages = (int)d->n_pages;
         at.fault = d->fault;
         at.layer = l; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;
-        at.split_tokens = o.split_tokens; at.n_splits = d->n_splits;
+        at.split_tokens = o.split_tokens; at.n_splits = d->n_splits; at.q_chunk = d->attn_qc; at.grouped = grouped;
+        at.q_block = d->attn_qb;
         at.scale = 1.0f / sqrtf((float)hd);
         at.part = d->part; at.counters = d->counters;
         if (!gemv_only) {
@@ -731,6 +741,12 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
     int bucket = 1;
     while (bucket < n) bucket <<= 1;
     if (bucket > B) bucket = B;
+    // a prefill group (consecutive positions of one session) selects the
+    // step variant whose attention shares K / V loads within the group
+    bool grouped = false;
+    for (int i = 1; i < n && d->attn_grouped && !grouped; i++)
+        grouped = cols[i].slot == cols[i - 1].slot && cols[i].pos == cols[i - 1].pos + 1 && cols[i - 1].pos >= 0;
+    const int gkey = bucket * 2 + (grouped ? 1 : 0);
     int *m = d->meta_host;
     for (int i = 0; i < B; i++) {
         bool live = i < n;
@@ -750,11 +766,11 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
     if (e == cudaSuccess) e = cudaEventRecord(d->ev0, d->stream);
     int launches = 0;
     if (e == cudaSuccess) {
-        auto it = d->graphs.find(bucket);
+        auto it = d->graphs.find(gkey);
         if (!opt_.use_graphs || it == d->graphs.end()) {
             // eager launches: always the first step of a bucket (sets kernel
             // attributes outside any capture), every step without graphs
-            e = record_step(d, opt_, bucket, max_pages_, launches);
+            e = record_step(d, opt_, bucket, max_pages_, launches, false, grouped);
             d->launches = launches;
             if (e == cudaSuccess && opt_.use_graphs) {
                 // capture this bucket for the next steps (capture does not run)
@@ -763,13 +779,13 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
                 int l2 = 0;
                 e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
                 if (e == cudaSuccess) {
-                    cudaError_t re = record_step(d, opt_, bucket, max_pages_, l2);
+                    cudaError_t re = record_step(d, opt_, bucket, max_pages_, l2, false, grouped);
                     e = cudaStreamEndCapture(d->stream, &g);
                     if (re != cudaSuccess) e = re;
                 }
                 if (e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
                 if (g) cudaGraphDestroy(g);
-                if (e == cudaSuccess) d->graphs[bucket] = ge;
+                if (e == cudaSuccess) d->graphs[gkey] = ge;
             }
         } else {
             e = cudaGraphLaunch(it->second, d->stream);

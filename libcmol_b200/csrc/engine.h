@@ -23,6 +23,7 @@ struct EngineOptions {
     float kv_pool_frac = 0.85f;
     bool  use_graphs = true;
     int   split_tokens = 64;   // attention context split (tokens per work item)
+    int   max_group = 1;       // most columns of one session in a step (prefill chunk)
 };
 
 struct SamplerParams {

@@ -217,6 +217,44 @@ def test_long_context_pages_and_splits(gpu, tmp_path, name):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("env", [{}, {"CMOLCU_ATTN_QB": "5"}, {"CMOLCU_ATTN_GROUP": "0"}],
+                         ids=["leaders32", "leaders5", "per_column"])
+@pytest.mark.parametrize("name", ["q8_0", "smollm3"])
+def test_batched_prefill_long_prompts(gpu, tmp_path, monkeypatch, name, env):
+    """Prompts of 300 and 170 tokens fed in chunks of up to 256 columns a step
+    next to each other's columns: each chunk is one attention group whose
+    block leaders (every 32 positions by default, 5 forced, or none) serve
+    all its queries from one K / V load per split.  The greedy continuations
+    equal the reference's for each prompt alone."""
+    from libcmol_b200 import synth
+    from libcmol_b200.model import GenParams, Model
+    from oracle.oracle import GenParams as OGenParams
+    from oracle.oracle import OracleModel
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    kw = dict(MODEL_KW[name])
+    dt = kw.pop("dtype")
+    path = str(tmp_path / f"prefill_{name}.gguf")
+    synth.write_gguf(path, synth.tiny_spec(dt, ctx=512, **kw))
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 512, size=300).astype(np.int32), rng.integers(0, 512, size=170).astype(np.int32)]
+    om = OracleModel(path, lanes=16)
+    want = []
+    for pr in prompts:
+        os_ = om.session(512)
+        ids, _ = om.generate_ids(os_, pr, OGenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=8))
+        want.append(ids.tolist())
+        om.free_session(os_)
+    with Model(path, max_ctx=512, max_sessions=2) as m:
+        ss = [m.acquire() for _ in prompts]
+        got = m.generate_batch(ss, prompts, [GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=8)] * 2)
+        assert [g.tolist() for g in got] == want
+        for s, pr, w in zip(ss, prompts, want):
+            assert s.n_tokens == len(pr) + len(w) - 1
+            s.release()
+
+
+@pytest.mark.gpu
 def test_stop_rules_and_session_state(gpu, paths):
     from libcmol_b200.model import GenParams, Model
     with Model(paths["q8_0"], max_ctx=32, max_sessions=2) as m:
