@@ -86,6 +86,7 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
         }
         sh.ok = ok;
     }
+    __syncwarp();   // warp 0 re-converges before the CTA barrier (which counts whole warps)
     for (int i = tid; i < G * hd; i += ATTN_THREADS)
         Qs[i] = __ldcg(a.q + (long long)col * a.q_ld + (long long)hk * G * hd + i);
     named_bar_sync(1, ATTN_THREADS);

@@ -2,12 +2,16 @@
 #include "gemm_tc.cuh"
 #include "gemv_launch.cuh"
 
+#include <cuda.h>        // CUtensorMap (the encode call is reached through the runtime)
+#include <stdlib.h>
+
 #include <algorithm>
 
-#define TC_DQW 8                          // dequantising warps (2..9)
-#define TC_THREADS ((2 + TC_DQW) * 32)    // + producer warp 0, MMA warp 1
+#define TC_DQW 8                          // dequantising warps (3..10)
+#define TC_THREADS ((3 + TC_DQW) * 32)    // + weight producer warp 0, MMA warp 1, activation producer warp 2
 #define TC_DQT (TC_DQW * 32)
 #define TC_MAX_DEPTH 8
+#define TC_RU 4                           // split-K reduction: tasks per thread in flight
 
 bool tc_supported(int dt) { return dt == DT_Q4_K || dt == DT_Q8_0 || dt == DT_Q4_0 || dt == DT_Q5_0; }
 
@@ -54,16 +58,6 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// 16-byte asynchronous copy global -> shared through the load/store unit,
-// and the arrival of this thread on `bar` once its earlier copies landed
-// (the mbarrier counts one arrival per issuing thread).
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -124,6 +118,9 @@ __global__ void __launch_bounds__(256) k_tc_xprep(const float *x, long long x_ld
 #define TC_MAX_QD 4        // quantised-stage ring depth
 
 struct TcParams {
+    // per plane: the full K-chunks as a 3-D tensor (bytes of a row's chunk,
+    // rows, chunk) and the last K-chunk as its own (its rows are shorter)
+    CUtensorMap     tm_full[3], tm_last[3];
     GemvArgs        g;                 // weight, y, epilogue fields
     int             epi, ncol, npad;
     const uint16_t *xs;
@@ -136,18 +133,23 @@ struct TcParams {
     int             qdepth;            // quantised-stage ring depth (<= TC_MAX_QD)
 };
 
-// Row stride, in a quantised stage, of plane p of format DT for one 256-value
-// slice: the slice's bytes rounded to 16, then to an odd multiple of 16 so
-// that the 8 lanes of a shared-memory phase reading 8 consecutive rows hit 8
-// different 16-byte bank groups.
-__host__ __device__ constexpr int tc_sp(int dt, int p) {
-    const int b = dt == DT_Q8_0 ? (p == 0 ? 256 : p == 1 ? 16 : 0)
-                : dt == DT_Q5_0 ? (p == 0 ? 128 : p == 1 ? 16 : p == 2 ? 32 : 0)
-                : (p == 0 ? 128 : p == 1 ? 16 : 0);          // Q4_0, Q4_K
-    return b == 0 ? 0 : ((b / 16) % 2 == 0 ? b + 16 : b);
-}
-__host__ __device__ constexpr int tc_stage_bytes(int dt) {
-    return TC_M * (tc_sp(dt, 0) + tc_sp(dt, 1) + tc_sp(dt, 2));
+// A quantised stage holds one 256-value slice of 128 rows, loaded by TMA
+// tensor copies (one per plane; Q8_0's 256-byte plane-0 rows as two
+// 128-byte boxes).  Plane 0 lands with the 128-byte swizzle: 16-byte chunk c
+// of row r sits at chunk c ^ (r % 8) of the row's 128 bytes, so the 8 lanes
+// of a shared-memory phase reading consecutive rows hit 8 bank groups.
+// Planes 1 (16 bytes a row: the block scales, or Q4_K's d, dmin and 6-bit
+// scales) and 2 (Q5_0's high bits, 32 bytes) are dense rows.
+__host__ __device__ constexpr int tc_nb0(int dt) { return dt == DT_Q8_0 ? 2 : 1; }
+__host__ __device__ constexpr int tc_p2b(int dt) { return dt == DT_Q5_0 ? 32 : 0; }
+__host__ __device__ constexpr int tc_off1(int dt) { return tc_nb0(dt) * TC_M * 128; }
+__host__ __device__ constexpr int tc_off2(int dt) { return tc_off1(dt) + TC_M * 16; }
+__host__ __device__ constexpr int tc_stage_tx(int dt) { return tc_off2(dt) + TC_M * tc_p2b(dt); }
+__host__ __device__ constexpr int tc_stage_bytes(int dt) { return (tc_stage_tx(dt) + 1023) / 1024 * 1024; }
+
+// The 16 bytes at byte `bo` of row r's plane-0 slice.
+__device__ __forceinline__ const uint8_t *tc_q0(const uint8_t *st, int r, int bo) {
+    return st + (bo >> 7) * (TC_M * 128) + r * 128 + ((((bo >> 4) & 7) ^ (r & 7)) << 4);
 }
 
 // Slice t of the matrix: K-chunk j, value offset `off` in it, `len` values.
@@ -165,64 +167,86 @@ __host__ __device__ inline void tc_slice(const QWeight &w, int t, int &j, int &o
     }
 }
 
-// 16 dequantised values of row r, values [v, v + 16) of the K-chunk held in
-// the quantised stage (GGUF block arithmetic of src/quant.c:152-194), as 8
-// packed f16 pairs.  No conversion instructions: a small unsigned integer u
-// becomes the f16 1024 + u by placing it under the exponent bits 0x6400
-// (one byte permute per pair), and the f32 2^23 + u under 0x4B000000.
+// 32 dequantised values of row r, values [v, v + 32) of the slice held in
+// the quantised stage (v a multiple of 32: one Q8_0 / Q4_0 / Q5_0 block, or
+// one 32-value group of a Q4_K super-block; GGUF block arithmetic of
+// src/quant.c:152-194), as 16 packed f16 pairs.  No conversion
+// instructions: a small unsigned integer u becomes the f16 1024 + u by
+// placing it under the exponent bits 0x6400 (one byte permute per pair), and
+// the f32 2^23 + u under 0x4B000000.
 //   Q8_0, Q4_0, Q5_0: q is exact in f16 and the block scale d is an f16, so
-//                     d * q in f16 arithmetic is the f16 rounding of the exact
-//                     value (the same as rounding the f32 product).
-//   Q4_K:             d * sc * q - dmin * mn in f32 (sc, mn 6-bit), then f16.
+//                     (1024 + u - bias) * d in f16 arithmetic is the f16
+//                     rounding of the exact value d * q.
+//   Q4_K:             d * sc * q - dmin * mn in f32 (sc, mn 6-bit; pairs of
+//                     values in packed f32x2 arithmetic), then f16.
 __device__ __forceinline__ uint32_t h2_from_bytes(uint32_t w, uint32_t sel) {
     // bytes of w selected by sel into the low byte of each half, 0x64 above
     return __byte_perm(w, 0x64646464u, sel);
 }
 
+// f16 pair of a * q - m for the two f32 patterns 2^23 + q in b0, b1
+// (a2 = {a, a}, nm2 = {-m, -m}): the exact subtraction of 2^23, one fused
+// multiply-add per value, one rounding to f16.
+__device__ __forceinline__ uint32_t q4k_h2(uint32_t b0, uint32_t b1, uint64_t a2, uint64_t nm2) {
+    const uint64_t n23 = 0xCB000000CB000000ull;   // {-2^23, -2^23}
+    uint64_t v, r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(b0), "r"(b1));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(v) : "l"(v), "l"(n23));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(v), "l"(a2), "l"(nm2));
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(r));
+    return pack_h2(__uint_as_float(lo), __uint_as_float(hi));
+}
+
 template <int DT>
-__device__ __forceinline__ void tc_dequant16(const uint8_t *P0, const uint8_t *P1, const uint8_t *P2, int v,
-                                             uint32_t out[8]) {
+__device__ __forceinline__ void tc_dequant32(const uint8_t *st, int r, int v, uint32_t out[16]) {
+    const uint8_t *P1 = st + tc_off1(DT) + r * 16, *P2 = st + tc_off2(DT) + r * tc_p2b(DT);
     if constexpr (DT == DT_Q4_K) {
-        // one super-block per slice: v in [0, 256)
-        const int pj = v >> 6, half = (v >> 5) & 1, sub = (v >> 4) & 1;
-        const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + 32 * pj + 16 * sub);
+        // one super-block per slice: v in [0, 256); values v.. of pair pj,
+        // low nibbles for the pair's first 32 values, high for the second
+        const int pj = v >> 6, half = (v >> 5) & 1;
+        const uint4 p0 = *reinterpret_cast<const uint4 *>(tc_q0(st, r, 32 * pj));
+        const uint4 p1 = *reinterpret_cast<const uint4 *>(tc_q0(st, r, 32 * pj + 16));
         const uint4 h = *reinterpret_cast<const uint4 *>(P1);
         const float d = h2f((uint16_t)(h.x & 0xFFFF)), dmin = h2f((uint16_t)(h.x >> 16));
         float sc0, sc1, mn0, mn1;
         q4k_pair(h.y, h.z, h.w, pj, sc0, sc1, mn0, mn1);
         const float a = d * (half ? sc1 : sc0), m = dmin * (half ? mn1 : mn0);
-        const uint32_t w[4] = {pl.x, pl.y, pl.z, pl.w};
+        uint64_t a2, nm2;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(a2) : "f"(a));
+        asm("mov.b64 %0, {%1, %1};" : "=l"(nm2) : "f"(-m));
+        const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < 8; i++) {
             const uint32_t t = half ? ((w[i] >> 4) & 0x0F0F0F0Fu) : (w[i] & 0x0F0F0F0Fu);
-            float f[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                f[j] = __fmaf_rn(a, __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7540u | j)) - 8388608.0f, -m);
-            out[2 * i] = pack_h2(f[0], f[1]);
-            out[2 * i + 1] = pack_h2(f[2], f[3]);
+            out[2 * i] = q4k_h2(__byte_perm(t, 0x4B000000u, 0x7540u), __byte_perm(t, 0x4B000000u, 0x7541u), a2, nm2);
+            out[2 * i + 1] = q4k_h2(__byte_perm(t, 0x4B000000u, 0x7542u), __byte_perm(t, 0x4B000000u, 0x7543u), a2, nm2);
         }
     } else {
-        const int b = v >> 5, hh = (v >> 4) & 1;
-        uint32_t w[4];
+        const int b = v >> 5;
+        uint32_t w[8];
         __half bias;
-        __half d;
+        const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
         if constexpr (DT == DT_Q8_0) {
-            const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 32 + 16 * hh);
-            d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
-            w[0] = pl.x ^ 0x80808080u; w[1] = pl.y ^ 0x80808080u;      // int8 -> unsigned + 128
-            w[2] = pl.z ^ 0x80808080u; w[3] = pl.w ^ 0x80808080u;
+            const uint4 p0 = *reinterpret_cast<const uint4 *>(tc_q0(st, r, b * 32));
+            const uint4 p1 = *reinterpret_cast<const uint4 *>(tc_q0(st, r, b * 32 + 16));
+            const uint32_t raw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) w[i] = raw[i] ^ 0x80808080u;   // int8 -> unsigned + 128
             bias = __ushort_as_half((uint16_t)0x6480);                  // 1024 + 128
         } else {
-            const uint4 pl = *reinterpret_cast<const uint4 *>(P0 + b * 16);
-            d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(P1 + b * 2));
+            // 16 bytes: value i in the low nibble of byte i, value 16 + i in the high
+            const uint4 pl = *reinterpret_cast<const uint4 *>(tc_q0(st, r, b * 16));
             const uint32_t raw[4] = {pl.x, pl.y, pl.z, pl.w};
 #pragma unroll
-            for (int i = 0; i < 4; i++) w[i] = hh ? ((raw[i] >> 4) & 0x0F0F0F0Fu) : (raw[i] & 0x0F0F0F0Fu);
+            for (int i = 0; i < 4; i++) {
+                w[i] = raw[i] & 0x0F0F0F0Fu;
+                w[4 + i] = (raw[i] >> 4) & 0x0F0F0F0Fu;
+            }
             if constexpr (DT == DT_Q5_0) {
                 const uint32_t qh = *reinterpret_cast<const uint32_t *>(P2 + b * 4);
 #pragma unroll
-                for (int i = 0; i < 4; i++) w[i] |= spread4_bit4((qh >> (16 * hh + 4 * i)) & 15u);
+                for (int i = 0; i < 8; i++) w[i] |= spread4_bit4((qh >> (4 * i)) & 15u);
                 bias = __ushort_as_half((uint16_t)0x6410);              // 1024 + 16
             } else {
                 bias = __ushort_as_half((uint16_t)0x6408);              // 1024 + 8
@@ -230,7 +254,7 @@ __device__ __forceinline__ void tc_dequant16(const uint8_t *P0, const uint8_t *P
         }
         const __half2 b2 = __halves2half2(bias, bias), d2 = __halves2half2(d, d);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < 8; i++) {
             const uint32_t lo = h2_from_bytes(w[i], 0x5140u), hi = h2_from_bytes(w[i], 0x5342u);
             __half2 x0 = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), b2), d2);
             __half2 x1 = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), b2), d2);
@@ -238,6 +262,16 @@ __device__ __forceinline__ void tc_dequant16(const uint8_t *P0, const uint8_t *P
             out[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&x1);
         }
     }
+}
+
+// TMA tensor copy of one box at (x, y, z) of `map` into shared memory,
+// completing in bytes on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // Epilogue of one value (STORE, RESID) or of a row pair (SWIGLU, QKV; the
@@ -271,8 +305,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     const int m0 = rb * TC_M;
     const int npad = p.npad;
     const int s0 = ks * p.slices_per_split, s1 = min(p.nslice, s0 + p.slices_per_split);
-    constexpr int SP0 = tc_sp(DT, 0), SP1 = tc_sp(DT, 1), SP2 = tc_sp(DT, 2);
-    constexpr int QOFF1 = TC_M * SP0, QOFF2 = TC_M * (SP0 + SP1), QB = tc_stage_bytes(DT);
+    constexpr int QB = tc_stage_bytes(DT);
 
     // shared memory: A tiles, B tiles (1024-aligned), quantised stages, barriers
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
@@ -288,7 +321,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
 
     if (tid == 0) {
         for (int i = 0; i < QD; i++) {
-            mbar_init(&qfull[i], 32);       // one cp.async arrival per producer lane
+            mbar_init(&qfull[i], 1);        // the producer's arrival with the stage's byte count
             mbar_init(&qempty[i], TC_DQW);
         }
         for (int i = 0; i < D; i++) {
@@ -321,39 +354,37 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     }
 
     if (warp == 0) {
-        // ---------------- producer: quantised slices (all lanes) and activation blocks (lane 0) --------
-        const int nrow = min(TC_M, w.prow - m0);
-        int bn = 0;
-        bool ok = true;
-        for (int t = s0; t < s1 && ok; t++) {
-            const int li = t - s0, stg = li % QD, use = li / QD;
-            if (use > 0 && !mbar_wait(&qempty[stg], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
-            int j, off, len;
-            tc_slice(w, t, j, off, len);
-            // 16-byte chunks of every row of every plane (consecutive lanes take
-            // consecutive chunks of a row: coalesced reads of the K-chunk-major planes)
-            const int c0 = round16(qw_plane_bytes(DT, 0, len)) / 16;
-            const int c1 = round16(qw_plane_bytes(DT, 1, len)) / 16;
-            const int c2 = DT == DT_Q5_0 ? round16(qw_plane_bytes(DT, 2, len)) / 16 : 0;
-            const int o0 = qw_plane_bytes(DT, 0, off), o1 = qw_plane_bytes(DT, 1, off), o2 = qw_plane_bytes(DT, 2, off);
-            uint8_t *q = Q + (size_t)stg * QB;
-            for (int idx = lane; idx < nrow * c0; idx += 32) {
-                const int r = idx / c0, c = idx % c0;
-                cp_async16(q + r * SP0 + 16 * c, qw_row(w, 0, j, m0 + r) + o0 + 16 * c);
+        // ---------------- weight producer: one TMA copy per plane and slice ----------------
+        // gated only by the dequantising warps releasing stages, so the ring
+        // runs QD slices ahead of the dequantisation
+        if (lane == 0) {
+            for (int t = s0; t < s1; t++) {
+                const int li = t - s0, stg = li % QD, use = li / QD;
+                if (use > 0 && !mbar_wait(&qempty[stg], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) break;
+                int j, off, len;
+                tc_slice(w, t, j, off, len);
+                const bool last = j == w.nkc - 1;
+                const CUtensorMap *mp = last ? p.tm_last : p.tm_full;
+                const int z = last ? 0 : j;
+                uint8_t *q = Q + (size_t)stg * QB;
+                const int o0 = qw_plane_bytes(DT, 0, off), o1 = qw_plane_bytes(DT, 1, off);
+                mbar_arrive_expect_tx(&qfull[stg], (uint32_t)tc_stage_tx(DT));
+#pragma unroll
+                for (int b = 0; b < tc_nb0(DT); b++) tma_load_3d(q + b * TC_M * 128, &mp[0], o0 + 128 * b, m0, z, &qfull[stg]);
+                tma_load_3d(q + tc_off1(DT), &mp[1], o1, m0, z, &qfull[stg]);
+                if constexpr (DT == DT_Q5_0)
+                    tma_load_3d(q + tc_off2(DT), &mp[2], qw_plane_bytes(DT, 2, off), m0, z, &qfull[stg]);
             }
-            for (int idx = lane; idx < nrow * c1; idx += 32) {
-                const int r = idx / c1, c = idx % c1;
-                cp_async16(q + QOFF1 + r * SP1 + 16 * c, qw_row(w, 1, j, m0 + r) + o1 + 16 * c);
-            }
-            if constexpr (DT == DT_Q5_0) {
-                for (int idx = lane; idx < nrow * c2; idx += 32) {
-                    const int r = idx / c2, c = idx % c2;
-                    cp_async16(q + QOFF2 + r * SP2 + 16 * c, qw_row(w, 2, j, m0 + r) + o2 + 16 * c);
-                }
-            }
-            cp_async_arrive(&qfull[stg]);
-            if (lane == 0) {
-                if (li == 0) pdl_wait();   // the activation image comes from the previous kernel
+        }
+    } else if (warp == 2) {
+        // ---------------- activation producer: one k-block of the image per tile slot ----------------
+        if (lane == 0) {
+            pdl_wait();   // the activation image comes from the previous kernel
+            int bn = 0;
+            bool ok = true;
+            for (int t = s0; t < s1 && ok; t++) {
+                int j, off, len;
+                tc_slice(w, t, j, off, len);
                 const int g0 = (j * w.kc + off) / TC_KB;
                 for (int i = 0; i < len / TC_KB; i++, bn++) {
                     const int slot = bn % D, u = bn / D;
@@ -363,7 +394,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                              &bfull[slot]);
                 }
             }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
     } else if (warp == 1) {
         // ---------------- MMA issue ----------------
@@ -385,7 +415,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         }
     } else {
         // ---------------- dequantise ----------------
-        const int dt = tid - 64;
+        const int dt = tid - 96;
         int i = 0;
         for (int t = s0; t < s1; t++) {
             const int li = t - s0, stg = li % QD;
@@ -397,15 +427,16 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                 const int slot = i % D, use = i / D;
                 if (use > 0) mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY);
                 uint8_t *tile = A + slot * TC_M * 128;
-                // task = (row r, 16-value run qq): 128 rows x 4 runs
-#pragma unroll
-                for (int tt = 0; tt < (TC_M * 4) / TC_DQT; tt++) {
-                    const int task = dt + TC_DQT * tt, r = task >> 2, qq = task & 3;
-                    uint32_t h[8];
-                    tc_dequant16<DT>(q + r * SP0, q + QOFF1 + r * SP1, q + QOFF2 + r * SP2, ib * TC_KB + 16 * qq, h);
+                // task = (row r, 32-value half hf): 128 rows x 2 halves, one per thread
+                static_assert(TC_M * 2 == TC_DQT, "one 32-value task per dequantising thread");
+                {
+                    const int r = dt >> 1, hf = dt & 1;
+                    uint32_t h[16];
+                    tc_dequant32<DT>(q, r, ib * TC_KB + 32 * hf, h);
                     uint4 *row = reinterpret_cast<uint4 *>(tile + r * 128);
-                    row[(2 * qq) ^ (r & 7)] = make_uint4(h[0], h[1], h[2], h[3]);
-                    row[(2 * qq + 1) ^ (r & 7)] = make_uint4(h[4], h[5], h[6], h[7]);
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+                        row[(4 * hf + c) ^ (r & 7)] = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
                 }
                 fence_proxy_async_smem();   // the tensor core reads the tile through the async proxy
                 __syncwarp();
@@ -415,8 +446,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
             if (lane == 0) mbar_arrive(&qempty[stg]);
         }
         // ---------------- epilogue: tensor memory -> registers ----------------
-        if (warp < 6) {
-            const int quarter = warp & 3;                 // the TMEM lanes this warp may read
+        if (warp < 7) {
+            const int quarter = warp & 3;                 // the TMEM lanes this warp may read (warps 3..6)
             const int row = m0 + 32 * quarter + lane;
             mbar_wait(accfull, 0, p.g.fault, FAULT_GEMV_FULL);
             tc_fence_after();
@@ -440,32 +471,61 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     }
 
     // ---------------- split-K: the last CTA of the row block adds the partials ----------------
+    // The roles above leave warps 0-2 diverged (lane 0 ran the loops); the
+    // CTA barrier counts whole warps, so each warp re-converges first.
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (p.ksplit > 1) {
         __threadfence();
         __syncthreads();
         if (tid == 0) s_last = atomicAdd(&p.counters[rb], 1) == p.ksplit - 1;
+        __syncwarp();
         __syncthreads();
         if (s_last) {
             __threadfence();
             pdl_wait();
-            // thread = (row pair, column): the even row's thread applies pair epilogues
-            for (int idx = tid; idx < (TC_M / 2) * npad; idx += TC_THREADS) {
-                const int rp = idx % (TC_M / 2), col = idx / (TC_M / 2);
-                const int r = 2 * rp;
-                float v0 = 0.f, v1 = 0.f;
-                for (int s = 0; s < p.ksplit; s++) {
-                    const float *pp = p.part + ((size_t)(rb * p.ksplit + s) * npad + col) * TC_M + r;
-                    v0 += __ldcg(pp);
-                    v1 += __ldcg(pp + 1);
+            // task = (column, 4 consecutive rows); a thread takes TC_RU tasks at
+            // once so that TC_RU float4 loads per split are in flight together.
+            // Partials add in split order (deterministic); the even row of a
+            // pair applies pair epilogues.
+            constexpr int RQ = TC_M / 4;
+            const int ntask = RQ * npad;
+            const float4 *P4 = reinterpret_cast<const float4 *>(p.part);
+            for (int base = tid; base < ntask; base += TC_RU * TC_THREADS) {
+                float4 acc[TC_RU];
+#pragma unroll
+                for (int u = 0; u < TC_RU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int sp = 0; sp < p.ksplit; sp++) {
+                    float4 v[TC_RU];
+#pragma unroll
+                    for (int u = 0; u < TC_RU; u++) {
+                        const int idx = base + u * TC_THREADS;
+                        const int rq = idx % RQ, col = idx / RQ;
+                        v[u] = idx < ntask ? __ldcg(P4 + (((size_t)(rb * p.ksplit + sp) * npad + col) * TC_M) / 4 + rq)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int u = 0; u < TC_RU; u++) {
+                        acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+                    }
                 }
-                const int row = m0 + r;
-                if (p.epi == EPI_STORE || p.epi == EPI_RESID) {
-                    tc_epilogue(p, row, col, v0, v1);
-                    tc_epilogue(p, row + 1, col, v1, v0);
-                } else {
-                    tc_epilogue(p, row, col, v0, v1);
+#pragma unroll
+                for (int u = 0; u < TC_RU; u++) {
+                    const int idx = base + u * TC_THREADS;
+                    if (idx >= ntask) continue;
+                    const int rq = idx % RQ, col = idx / RQ;
+                    const int row = m0 + 4 * rq;
+                    const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+                    for (int e = 0; e < 4; e += 2) {
+                        if (p.epi == EPI_STORE || p.epi == EPI_RESID) {
+                            tc_epilogue(p, row + e, col, a4[e], a4[e + 1]);
+                            tc_epilogue(p, row + e + 1, col, a4[e + 1], a4[e]);
+                        } else {
+                            tc_epilogue(p, row + e, col, a4[e], a4[e + 1]);
+                        }
+                    }
                 }
             }
             if (tid == 0) p.counters[rb] = 0;
@@ -485,16 +545,26 @@ static int tc_npad(int ncol) { return std::max(16, (ncol + 15) / 16 * 16); }
 // Ring depths and shared memory of one CTA: two CTAs share an SM when both
 // fit (<= 112 KB each, narrow batches); otherwise one CTA takes the SM and
 // deeper rings.
+// Tuning knobs read once per process (measurements): CMOLCU_TC_PER_SM=1
+// forces one CTA per SM, CMOLCU_TC_KSPLIT_MAX caps the split of K.
+static int tc_knob(const char *name, int dflt) {
+    const char *v = getenv(name);
+    return v && *v ? atoi(v) : dflt;
+}
+
 static void tc_rings(int dt, int npad, int &depth, int &qdepth, size_t &smem, int &per_sm) {
+    static const int max_per_sm = tc_knob("CMOLCU_TC_PER_SM", 2) == 1 ? 1 : 2;
     const size_t qb = (size_t)tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
     const size_t per_slot = (size_t)TC_M * 128 + (size_t)npad * 128;
-    for (per_sm = 2; per_sm >= 1; per_sm--) {
+    for (per_sm = max_per_sm; per_sm >= 1; per_sm--) {
         const long long budget = per_sm == 2 ? 112LL * 1024 : 220LL * 1024;
-        qdepth = per_sm == 2 ? 2 : 3;
-        const long long room = budget - 1024 - (long long)(qdepth * qb) - (long long)bars;
-        depth = (int)std::min<long long>(TC_MAX_DEPTH, room / (long long)per_slot);
-        smem = 1024 + (size_t)std::max(depth, 2) * per_slot + (size_t)qdepth * qb + bars;
-        if (depth >= 2 && (long long)smem <= budget) return;
+        // the deepest quantised ring that leaves a tile ring of >= 2
+        for (qdepth = TC_MAX_QD; qdepth >= 2; qdepth--) {
+            const long long room = budget - 1024 - (long long)(qdepth * qb) - (long long)bars;
+            depth = (int)std::min<long long>(TC_MAX_DEPTH, room / (long long)per_slot);
+            smem = 1024 + (size_t)std::max(depth, 2) * per_slot + (size_t)qdepth * qb + bars;
+            if (depth >= 2 && (long long)smem <= budget) return;
+        }
     }
     per_sm = 1;
     depth = 2;
@@ -509,9 +579,10 @@ static int tc_nslice(int k, int kc) {
 }
 
 static void tc_split(int rows, int nslice, int per_sm, int &rblocks, int &ksplit, int &sps) {
+    static const int cap = std::max(1, tc_knob("CMOLCU_TC_KSPLIT_MAX", 1 << 20));
     const int slots = device_sm_count() * per_sm;
     rblocks = (rows + TC_M - 1) / TC_M;
-    ksplit = std::max(1, std::min(nslice, slots / rblocks));    // one wave
+    ksplit = std::max(1, std::min(std::min(nslice, cap), slots / rblocks));    // one wave
     sps = (nslice + ksplit - 1) / ksplit;
     ksplit = (nslice + sps - 1) / sps;
 }
@@ -526,6 +597,53 @@ void tc_scratch_need(int rows, int k, int ncol, size_t *xs_halves, size_t *part_
 }
 
 typedef void (*tc_kernel_t)(TcParams);
+
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point
+// (no link-time dependency on the driver library).
+typedef CUresult (*tc_encode_t)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static tc_encode_t tc_encode_fn() {
+    static const tc_encode_t fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<tc_encode_t>(f);
+    }();
+    return fn;
+}
+
+// Tensor map of one plane: x = bytes of a row's K-chunk (16-byte multiple),
+// y = rows, z = K-chunks (`nz`, each rows * row_bytes apart); box
+// box_x bytes x 128 rows x 1, with the 128-byte swizzle for plane 0.  Boxes
+// reaching past the rows or a short chunk read zeros.
+static bool tc_plane_map(CUtensorMap *m, const uint8_t *base, int row_bytes, int rows, int nz, int box_x, bool swz) {
+    const tc_encode_t enc = tc_encode_fn();
+    if (!enc || row_bytes <= 0 || rows <= 0 || nz <= 0) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)rows, (cuuint64_t)nz};
+    const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)row_bytes * (cuuint64_t)rows};
+    const cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)TC_M, 1u};
+    const cuuint32_t es[3] = {1u, 1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The full-chunk and last-chunk maps of every plane the format has.
+static bool tc_weight_maps(const QWeight &w, TcParams &p) {
+    const int np = w.dtype == DT_Q5_0 ? 3 : 2;
+    for (int pl = 0; pl < np; pl++) {
+        const int box = pl == 0 ? 128 : pl == 1 ? 16 : 32;
+        if (w.nkc > 1 && !tc_plane_map(&p.tm_full[pl], w.p[pl], w.cs[pl], w.prow, w.nkc - 1, box, pl == 0))
+            return false;
+        const uint8_t *last = w.p[pl] + (size_t)(w.nkc - 1) * w.prow * w.cs[pl];
+        if (!tc_plane_map(&p.tm_last[pl], last, w.cl[pl], w.prow, 1, box, pl == 0)) return false;
+    }
+    return true;
+}
 
 static tc_kernel_t tc_pick(int dt) {
     switch (dt) {
@@ -567,6 +685,7 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     p.tmem_cols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
     p.depth = depth;
     p.qdepth = qdepth;
+    if (!tc_weight_maps(w, p)) return cudaErrorInvalidValue;
     static size_t attr_done[64][4];
     int dev = 0;
     cudaGetDevice(&dev);
