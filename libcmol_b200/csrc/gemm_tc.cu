@@ -6,6 +6,8 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <mutex>
+#include <vector>
 
 #define TC_DQW 8                          // dequantising warps (3..10)
 #define TC_THREADS ((3 + TC_DQW) * 32)    // + weight producer warp 0, MMA warp 1, activation producer warp 2
@@ -129,8 +131,11 @@ struct TcParams {
     float          *part;
     int            *counters;
     uint32_t        tmem_cols;
-    int             depth;             // A / B tile ring depth (<= TC_MAX_DEPTH)
+    int             depth;             // A (dequantised) tile ring depth (<= TC_MAX_DEPTH)
+    int             bdepth;            // B (activation) tile ring depth (<= TC_MAX_DEPTH)
     int             qdepth;            // quantised-stage ring depth (<= TC_MAX_QD)
+    int             cluster;           // 1: the K splits of a row block form one cluster and add
+                                       // their partials through distributed shared memory
 };
 
 // A quantised stage holds one 256-value slice of 128 rows, loaded by TMA
@@ -274,6 +279,27 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// Distributed shared memory: the address of shared offset `saddr` in the
+// cluster's CTA `rank`, a 16-byte load from it, and the cluster-wide barrier
+// (release / acquire: shared-memory writes before it are visible to every
+// CTA of the cluster after it).
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(a)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Epilogue of one value (STORE, RESID) or of a row pair (SWIGLU, QKV; the
 // even row's thread writes).
 __device__ __forceinline__ void tc_epilogue(const TcParams &p, int row, int col, float v, float partner) {
@@ -297,6 +323,50 @@ __device__ __forceinline__ void tc_epilogue(const TcParams &p, int row, int col,
     }
 }
 
+// Adds the split partials of this row block for columns [c_lo, c_hi) and
+// runs the epilogue.  Task = (column, 4 consecutive rows); a thread takes
+// TC_RU tasks at once so that TC_RU float4 loads per split are in flight
+// together.  Partials add in split order (deterministic); the even row of a
+// pair applies pair epilogues.  load(split, column, row quad) -> float4.
+template <typename LoadF>
+__device__ __forceinline__ void tc_reduce_cols(const TcParams &p, int m0, int c_lo, int c_hi, int tid, LoadF load) {
+    constexpr int RQ = TC_M / 4;
+    const int ntask = RQ * max(0, c_hi - c_lo);
+    for (int base = tid; base < ntask; base += TC_RU * TC_THREADS) {
+        float4 acc[TC_RU];
+#pragma unroll
+        for (int u = 0; u < TC_RU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < p.ksplit; sp++) {
+            float4 v[TC_RU];
+#pragma unroll
+            for (int u = 0; u < TC_RU; u++) {
+                const int idx = base + u * TC_THREADS;
+                v[u] = idx < ntask ? load(sp, c_lo + idx / RQ, idx % RQ) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < TC_RU; u++) {
+                acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < TC_RU; u++) {
+            const int idx = base + u * TC_THREADS;
+            if (idx >= ntask) continue;
+            const int col = c_lo + idx / RQ, row = m0 + 4 * (idx % RQ);
+            const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+                if (p.epi == EPI_STORE || p.epi == EPI_RESID) {
+                    tc_epilogue(p, row + e, col, a4[e], a4[e + 1]);
+                    tc_epilogue(p, row + e + 1, col, a4[e + 1], a4[e]);
+                } else {
+                    tc_epilogue(p, row + e, col, a4[e], a4[e + 1]);
+                }
+            }
+        }
+    }
+}
+
 template <int DT>
 __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant__ TcParams p) {
     const QWeight &w = p.g.w;
@@ -309,10 +379,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
 
     // shared memory: A tiles, B tiles (1024-aligned), quantised stages, barriers
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
-    const int D = p.depth, QD = p.qdepth;
+    const int D = p.depth, DB = p.bdepth, QD = p.qdepth;
     uint8_t *A = base;                                        // D x 16 KB
-    uint8_t *B = A + (size_t)D * TC_M * 128;                  // D x npad * 128
-    uint8_t *Q = B + (size_t)D * npad * 128;                  // QD x QB
+    uint8_t *B = A + (size_t)D * TC_M * 128;                  // DB x npad * 128
+    uint8_t *Q = B + (size_t)DB * npad * 128;                 // QD x QB
     uint64_t *bars = reinterpret_cast<uint64_t *>(Q + (size_t)QD * QB);
     uint64_t *accfull = bars, *qfull = bars + 1, *qempty = qfull + TC_MAX_QD, *afull = qempty + TC_MAX_QD,
              *aempty = afull + TC_MAX_DEPTH, *bfull = aempty + TC_MAX_DEPTH, *bempty = bfull + TC_MAX_DEPTH;
@@ -320,6 +390,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     __shared__ int s_last;
 
     if (tid == 0) {
+        // the weight's tensor maps, fetched while the rest of the setup runs
+#pragma unroll
+        for (int pl = 0; pl < (DT == DT_Q5_0 ? 3 : 2); pl++) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_last[pl])) : "memory");
+            if (w.nkc > 1)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_full[pl])) : "memory");
+        }
         for (int i = 0; i < QD; i++) {
             mbar_init(&qfull[i], 1);        // the producer's arrival with the stage's byte count
             mbar_init(&qempty[i], TC_DQW);
@@ -327,6 +404,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         for (int i = 0; i < D; i++) {
             mbar_init(&afull[i], TC_DQW);
             mbar_init(&aempty[i], 1);
+        }
+        for (int i = 0; i < DB; i++) {
             mbar_init(&bfull[i], 1);
             mbar_init(&bempty[i], 1);
         }
@@ -387,7 +466,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                 tc_slice(w, t, j, off, len);
                 const int g0 = (j * w.kc + off) / TC_KB;
                 for (int i = 0; i < len / TC_KB; i++, bn++) {
-                    const int slot = bn % D, u = bn / D;
+                    const int slot = bn % DB, u = bn / DB;
                     if (u > 0 && !mbar_wait(&bempty[slot], (u - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
                     mbar_arrive_expect_tx(&bfull[slot], (uint32_t)(npad * 128));
                     bulk_g2s(B + (size_t)slot * npad * 128, p.xs + (size_t)(g0 + i) * npad * 64, (uint32_t)(npad * 128),
@@ -400,16 +479,16 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | ((uint32_t)(npad >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
             for (int i = 0; i < nkb; i++) {
-                const int slot = i % D, use = i / D;
+                const int slot = i % D, use = i / D, bslot = i % DB, buse = i / DB;
                 mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
-                mbar_wait(&bfull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
+                mbar_wait(&bfull[bslot], buse & 1, p.g.fault, FAULT_GEMV_FULL);
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(A + slot * TC_M * 128), b_addr = smem_u32(B + (size_t)slot * npad * 128);
+                const uint32_t a_addr = smem_u32(A + slot * TC_M * 128), b_addr = smem_u32(B + (size_t)bslot * npad * 128);
 #pragma unroll
                 for (int k = 0; k < TC_KB / 16; k++)
                     tc_mma(tmem, tc_desc(a_addr + 32 * k), tc_desc(b_addr + 32 * k), idesc, (i | k) != 0);
                 tc_commit(&aempty[slot]);
-                tc_commit(&bempty[slot]);
+                tc_commit(&bempty[bslot]);
             }
             tc_commit(accfull);
         }
@@ -462,7 +541,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                         tc_epilogue(p, row, c0 + e, v[e], partner);
                     }
                 } else {
-                    float *pp = p.part + ((size_t)(rb * p.ksplit + ks) * npad + c0) * TC_M + (row - m0);
+                    // partial sums: [column][row] in this CTA's shared memory (the
+                    // rings are drained: every copy and MMA has completed) or in
+                    // global scratch
+                    float *pp = p.cluster ? reinterpret_cast<float *>(base) + (size_t)c0 * TC_M + (row - m0)
+                                          : p.part + ((size_t)(rb * p.ksplit + ks) * npad + c0) * TC_M + (row - m0);
 #pragma unroll
                     for (int e = 0; e < 16; e++) pp[(size_t)e * TC_M] = v[e];
                 }
@@ -470,13 +553,26 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         }
     }
 
-    // ---------------- split-K: the last CTA of the row block adds the partials ----------------
+    // ---------------- split-K: the partials of the row block's K splits are added ----------------
     // The roles above leave warps 0-2 diverged (lane 0 ran the loops); the
     // CTA barrier counts whole warps, so each warp re-converges first.
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (p.ksplit > 1) {
+    if (p.ksplit > 1 && p.cluster) {
+        // every CTA of the cluster has its partial in shared memory; CTA s adds
+        // columns [s * cw, (s + 1) * cw) over the cluster, in split order
+        cluster_sync_all();
+        pdl_wait();
+        const int cw = (npad + p.ksplit - 1) / p.ksplit;
+        const int c_lo = ks * cw, c_hi = min(npad, c_lo + cw);
+        const uint32_t ps = smem_u32(base);
+        tc_reduce_cols(p, m0, c_lo, c_hi, tid, [&](int sp, int col, int rq) {
+            return ld_dsmem_f4(dsmem_addr(ps + (uint32_t)((col * TC_M + 4 * rq) * 4), (uint32_t)sp));
+        });
+        cluster_sync_all();   // the partials stay in place until every CTA has read them
+    } else if (p.ksplit > 1) {
+        // the last CTA of the row block (atomic counter) adds the global partials
         __threadfence();
         __syncthreads();
         if (tid == 0) s_last = atomicAdd(&p.counters[rb], 1) == p.ksplit - 1;
@@ -485,49 +581,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         if (s_last) {
             __threadfence();
             pdl_wait();
-            // task = (column, 4 consecutive rows); a thread takes TC_RU tasks at
-            // once so that TC_RU float4 loads per split are in flight together.
-            // Partials add in split order (deterministic); the even row of a
-            // pair applies pair epilogues.
-            constexpr int RQ = TC_M / 4;
-            const int ntask = RQ * npad;
             const float4 *P4 = reinterpret_cast<const float4 *>(p.part);
-            for (int base = tid; base < ntask; base += TC_RU * TC_THREADS) {
-                float4 acc[TC_RU];
-#pragma unroll
-                for (int u = 0; u < TC_RU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int sp = 0; sp < p.ksplit; sp++) {
-                    float4 v[TC_RU];
-#pragma unroll
-                    for (int u = 0; u < TC_RU; u++) {
-                        const int idx = base + u * TC_THREADS;
-                        const int rq = idx % RQ, col = idx / RQ;
-                        v[u] = idx < ntask ? __ldcg(P4 + (((size_t)(rb * p.ksplit + sp) * npad + col) * TC_M) / 4 + rq)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-#pragma unroll
-                    for (int u = 0; u < TC_RU; u++) {
-                        acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < TC_RU; u++) {
-                    const int idx = base + u * TC_THREADS;
-                    if (idx >= ntask) continue;
-                    const int rq = idx % RQ, col = idx / RQ;
-                    const int row = m0 + 4 * rq;
-                    const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-#pragma unroll
-                    for (int e = 0; e < 4; e += 2) {
-                        if (p.epi == EPI_STORE || p.epi == EPI_RESID) {
-                            tc_epilogue(p, row + e, col, a4[e], a4[e + 1]);
-                            tc_epilogue(p, row + e + 1, col, a4[e + 1], a4[e]);
-                        } else {
-                            tc_epilogue(p, row + e, col, a4[e], a4[e + 1]);
-                        }
-                    }
-                }
-            }
+            tc_reduce_cols(p, m0, 0, npad, tid, [&](int sp, int col, int rq) {
+                return __ldcg(P4 + (((size_t)(rb * p.ksplit + sp) * npad + col) * TC_M) / 4 + rq);
+            });
             if (tid == 0) p.counters[rb] = 0;
         }
     }
@@ -552,24 +609,35 @@ static int tc_knob(const char *name, int dflt) {
     return v && *v ? atoi(v) : dflt;
 }
 
-static void tc_rings(int dt, int npad, int &depth, int &qdepth, size_t &smem, int &per_sm) {
+// Ring depths and shared memory of one CTA.  Two CTAs share an SM when the
+// minimum rings fit in ~112 KB (narrow batches); otherwise one CTA takes the
+// SM.  Spare room deepens, in this order: the activation ring (its tiles
+// are small at narrow batches, and a shallow one puts an L2 round trip
+// behind every k-block's MMA), the dequantised ring, the quantised ring.
+static void tc_rings(int dt, int npad, int &depth, int &bdepth, int &qdepth, size_t &smem, int &per_sm) {
     static const int max_per_sm = tc_knob("CMOLCU_TC_PER_SM", 2) == 1 ? 1 : 2;
     const size_t qb = (size_t)tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
-    const size_t per_slot = (size_t)TC_M * 128 + (size_t)npad * 128;
+    const size_t a_slot = (size_t)TC_M * 128, b_slot = (size_t)npad * 128;
+    auto need = [&](int da, int db, int dq) { return 1024 + da * a_slot + db * b_slot + dq * qb + bars; };
     for (per_sm = max_per_sm; per_sm >= 1; per_sm--) {
-        const long long budget = per_sm == 2 ? 112LL * 1024 : 220LL * 1024;
-        // the deepest quantised ring that leaves a tile ring of >= 2
-        for (qdepth = TC_MAX_QD; qdepth >= 2; qdepth--) {
-            const long long room = budget - 1024 - (long long)(qdepth * qb) - (long long)bars;
-            depth = (int)std::min<long long>(TC_MAX_DEPTH, room / (long long)per_slot);
-            smem = 1024 + (size_t)std::max(depth, 2) * per_slot + (size_t)qdepth * qb + bars;
-            if (depth >= 2 && (long long)smem <= budget) return;
+        const size_t budget = per_sm == 2 ? 112 * 1024 : 220 * 1024;
+        depth = bdepth = qdepth = 2;
+        if (need(2, 2, 2) > budget && per_sm == 2) continue;
+        const int steps[][3] = {{0, 4, 0}, {3, 0, 0}, {0, 0, 3}, {0, 8, 0}, {4, 0, 0}, {0, 0, 4}};
+        for (const auto &st : steps) {
+            const int da = std::max(depth, st[0]), db = std::max(bdepth, st[1]), dq = std::max(qdepth, st[2]);
+            for (int b = db; b >= bdepth; b--)     // as deep a B ring as fits at this step
+                if (need(da, b, dq) <= budget) {
+                    depth = da; bdepth = b; qdepth = dq;
+                    break;
+                }
         }
+        smem = need(depth, bdepth, qdepth);
+        return;
     }
     per_sm = 1;
-    depth = 2;
-    qdepth = 2;
-    smem = 1024 + 2 * per_slot + 2 * qb + bars;
+    depth = bdepth = qdepth = 2;
+    smem = need(2, 2, 2);
 }
 
 static int tc_nslice(int k, int kc) {
@@ -597,6 +665,69 @@ void tc_scratch_need(int rows, int k, int ncol, size_t *xs_halves, size_t *part_
 }
 
 typedef void (*tc_kernel_t)(TcParams);
+
+#define TC_MAX_CLUSTER 16    // K splits of a row block that may form one cluster (8 portable)
+
+// True when `ks` CTAs of `smem` bytes can run as one (1, ks, 1) cluster of
+// kernel k on this device (cached per kernel, size and device).
+static bool tc_cluster_ok(tc_kernel_t k, int ks, int rb, size_t smem) {
+    struct Entry { tc_kernel_t k; int ks, dev; size_t smem; bool ok; };
+    static std::vector<Entry> cache;
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    for (const Entry &e : cache)
+        if (e.k == k && e.ks == ks && e.dev == dev && e.smem == smem) return e.ok;
+    bool ok = ks >= 2 && ks <= TC_MAX_CLUSTER;
+    if (ok && ks > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        ok = false;
+    if (ok) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(rb, ks);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 1;
+        at[0].val.clusterDim.y = ks;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        ok = cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess && n >= 1;
+    }
+    cudaGetLastError();   // a refused query leaves no sticky error
+    cache.push_back({k, ks, dev, smem, ok});
+    return ok;
+}
+
+// The matmul launch: PDL, and a (1, cluster_y, 1) cluster when cluster_y > 1.
+static cudaError_t tc_launch(tc_kernel_t k, dim3 grid, size_t smem, cudaStream_t st, bool pdl, int cluster_y,
+                             const TcParams &p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (cluster_y > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = cluster_y;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k, p);
+}
 
 // cuTensorMapEncodeTiled, reached through the runtime's driver entry point
 // (no link-time dependency on the driver library).
@@ -662,9 +793,9 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     if (w.nkc > 1 && w.kc % TC_SV) return cudaErrorInvalidValue;
     if (w.dtype == DT_Q4_K && w.k % TC_SV) return cudaErrorInvalidValue;
     const int npad = tc_npad(ncol);
-    int depth, qdepth, per_sm;
+    int depth, bdepth, qdepth, per_sm;
     size_t smem;
-    tc_rings(w.dtype, npad, depth, qdepth, smem, per_sm);
+    tc_rings(w.dtype, npad, depth, bdepth, qdepth, smem, per_sm);
     const int nslice = tc_nslice(w.k, w.kc);
     int rb, ks, sps;
     tc_split(w.rows, nslice, per_sm, rb, ks, sps);
@@ -684,6 +815,7 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     p.counters = s.counters;
     p.tmem_cols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
     p.depth = depth;
+    p.bdepth = bdepth;
     p.qdepth = qdepth;
     if (!tc_weight_maps(w, p)) return cudaErrorInvalidValue;
     static size_t attr_done[64][4];
@@ -704,8 +836,13 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
         attr_done[dev][di] = lim;
     }
     if (smem > attr_done[dev][di]) return cudaErrorInvalidConfiguration;
+    // split partials through distributed shared memory when the splits fit in
+    // one cluster and a partial ([npad][128] floats) fits in the drained rings
+    const size_t rings = (size_t)depth * TC_M * 128 + (size_t)bdepth * npad * 128 + (size_t)qdepth * tc_stage_bytes(w.dtype);
+    static const bool no_cluster = tc_knob("CMOLCU_TC_CLUSTER", 1) == 0;
+    p.cluster = !no_cluster && ks > 1 && (size_t)npad * TC_M * 4 <= rings && tc_cluster_ok(k, ks, rb, smem) ? 1 : 0;
     cudaError_t e = launch_k(k_tc_xprep, dim3(npad), dim3(256), 0, st, pdl, a.x, a.x_ld, w.k, ncol, npad, a.norm_w,
                              a.eps, s.xs);
     if (e != cudaSuccess) return e;
-    return launch_k(k, dim3(rb, ks), dim3(TC_THREADS), smem, st, pdl, p);
+    return tc_launch(k, dim3(rb, ks), smem, st, pdl, p.cluster ? ks : 1, p);
 }

@@ -75,3 +75,28 @@ def test_batched_rejects_unsupported(gpu):
     with pytest.raises(CmolError, match="tensor-core"):
         W.matmul_batched(x, y, 16)
     W.free()
+
+
+@pytest.mark.gpu
+def test_batched_global_partials(gpu):
+    """With clusters off (CMOLCU_TC_CLUSTER=0, read once per process) the K
+    splits add their partials through global scratch and the last CTA of the
+    row block; same bound, in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = f"""
+import sys
+sys.path.insert(0, {os.path.dirname(here)!r})
+sys.path.insert(0, {here!r})
+import torch
+import test_gemm_tc_gpu as t
+dev = torch.device("cuda:0")
+for case in [t.CASES[0], t.CASES[4], t.CASES[6]]:
+    t.test_batched_matches_exact(dev, *case, norm=True)
+print("ok")
+"""
+    env = dict(os.environ, CMOLCU_TC_CLUSTER="0")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
