@@ -1,6 +1,9 @@
 // gemv.cu — template instances, launch planning and weight repacking.
 #include "gemv_launch.cuh"
 
+#include <stdio.h>
+#include <stdlib.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -153,6 +156,24 @@ static void fmt_of(int dt, int &vpc, int &cr) {
 // next kernel of the step can start streaming while this one drains.  Large
 // matrices use one CTA per SM with up to ~216 KB, so an SM's whole share (or
 // most of it) is in flight at once.
+// CMOLCU_GEMV_PLAN=<kb>:<ctas per SM> (measurements) forces one budget
+// and grid for every launch, e.g. 100:1 (the narrow variant, one CTA per SM,
+// so that the next kernel's CTAs fit beside this one's).
+static void gemv_forced_plan(int &kb, int &per_sm) {
+    static int fkb = -1, fps = 0;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char *v = getenv("CMOLCU_GEMV_PLAN");
+        int a = 0, b = 0;
+        if (v && sscanf(v, "%d:%d", &a, &b) == 2 && (a == 100 || a == 216) && b >= 1 && b <= 2) {
+            fkb = a;
+            fps = b;
+        }
+    });
+    kb = fkb;
+    per_sm = fps;
+}
+
 bool gemv_plan(const QWeight &w, int nc, PipeCfg &pc, int &R, int &grid) {
     const int sms = device_sm_count();
     R = 4;
@@ -160,8 +181,10 @@ bool gemv_plan(const QWeight &w, int nc, PipeCfg &pc, int &R, int &grid) {
     fmt_of(w.dtype, vpc, cr);
     const size_t xb = gemv_x_bytes(nc, w.k, vpc, cr);
     const bool large = w.bytes >= (size_t)4 << 20;
-    const int order[2][2] = {{100, 216}, {216, 100}};
-    for (int budget_kb : order[large ? 1 : 0]) {
+    int forced_kb = -1, forced_per_sm = 0;
+    gemv_forced_plan(forced_kb, forced_per_sm);
+    const int order[3][2] = {{100, 216}, {216, 100}, {forced_kb, forced_kb == 100 ? 216 : 100}};
+    for (int budget_kb : order[forced_kb > 0 ? 2 : large ? 1 : 0]) {
         // one CTA per SM gets the wide variant (15 consumer warps)
         const int cw = budget_kb <= 100 ? GEMV_CWARPS : GEMV_CWARPS_WIDE;
         const int tr = cw * R;
@@ -174,7 +197,7 @@ bool gemv_plan(const QWeight &w, int nc, PipeCfg &pc, int &R, int &grid) {
         pc.cw = cw;
         const long long avail = (long long)budget_kb * 1024 - (long long)xb - 2 * GEMV_MAX_STAGES * 8;
         if (avail < 2LL * pc.sb) continue;
-        const int ctas = sms * (budget_kb <= 100 ? 2 : 1);
+        const int ctas = sms * (forced_per_sm > 0 && budget_kb == forced_kb ? forced_per_sm : budget_kb <= 100 ? 2 : 1);
         int rpc = (w.rows + ctas - 1) / ctas;
         rpc = (rpc + R - 1) / R * R;
         pc.rows_per_cta = rpc;
