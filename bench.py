@@ -57,16 +57,14 @@ WORKLOADS["c4"] = dict(cfg=4, sessions=256, prompt=(32, 8192), gen=(256, 256), s
 GEMV_M, GEMV_K = 11008, 2048
 
 
-def run_batched(args, rank, world, local, barrier, dist=None):
-    """Configs 3 and 4: many ragged sessions at once through cmol_generate_batch
-    (one request per session, continuous batching on each GPU).  value =
-    generated tokens of all ranks / max over ranks of the device time of all
-    steps (prefill steps included); e2e = the same tokens over the wall time
-    of the cmol_generate_batch call (host buffers)."""
+def batched_plan(args, rank, world):
+    """This rank's share of a config 3 / 4 workload: session count, prompt and
+    generation lengths (seeded per rank), its context cap, the synthetic
+    model's spec and the generator (prompts are drawn from it next).  The
+    spec, and so the model file, is the same on every rank."""
     import numpy as np
 
     from libcmol_b200 import synth
-    from libcmol_b200.model import GenParams, Model
     wl = WORKLOADS[args.workload]
     sessions = wl["sessions"] if wl["cfg"] == 3 else max(1, sessions_per_rank(wl["sessions"], world, rank))
     if args.sessions > 0:
@@ -81,7 +79,25 @@ def run_batched(args, rank, world, local, barrier, dist=None):
     if args.prompt_scale != 1.0:
         plen = np.maximum(1, (plen * args.prompt_scale).astype(int))
     ctx = int(plen.max() + glen.max() + 8)
-    spec = synth.baseline_spec(wl["cfg"], ctx=max(ctx, 256))
+    # the model file is shared by the ranks: its context length comes from
+    # the workload's bounds (the same on every rank), not from this rank's draw
+    ctx_model = int(max(1, hi * args.prompt_scale) + wl["gen"][1] + 8)
+    spec = synth.baseline_spec(wl["cfg"], ctx=max(ctx, ctx_model, 256))
+    return sessions, plen, glen, ctx, spec, rng
+
+
+def run_batched(args, rank, world, local, barrier, dist=None):
+    """Configs 3 and 4: many ragged sessions at once through cmol_generate_batch
+    (one request per session, continuous batching on each GPU).  value =
+    generated tokens of all ranks / max over ranks of the device time of all
+    steps (prefill steps included); e2e = the same tokens over the wall time
+    of the cmol_generate_batch call (host buffers)."""
+    import numpy as np
+
+    from libcmol_b200 import synth
+    from libcmol_b200.model import GenParams, Model
+    wl = WORKLOADS[args.workload]
+    sessions, plen, glen, ctx, spec, rng = batched_plan(args, rank, world)
     path = ensure_model(spec, rank, barrier)
     V = spec.vocab_size
     prompts = [rng.integers(0, V, int(n)).astype(np.int32) for n in plen]
@@ -223,7 +239,9 @@ def ensure_model(spec, rank, barrier):
     from libcmol_b200 import synth
     path = model_path(spec)
     if rank == 0 and not os.path.exists(path):
-        synth.write_gguf(path, spec)
+        tmp = f"{path}.tmp{os.getpid()}"
+        synth.write_gguf(tmp, spec)
+        os.replace(tmp, path)      # readers never see a partial file
     barrier()
     return path
 

@@ -57,3 +57,20 @@ def test_single_rank_is_identity():
     assert bench.reduce_ranks(None, "cpu", sums=(1, 2), maxes=(3,)) == ([1.0, 2.0], [3.0])
     assert sum(bench.sessions_per_rank(256, 8, r) for r in range(8)) == 256
     assert sum(bench.sessions_per_rank(255, 8, r) for r in range(8)) == 255
+
+
+@pytest.mark.parametrize("workload", ["c3", "c4"])
+@pytest.mark.parametrize("scale", [1.0, 0.25])
+def test_ranks_share_one_model_file(workload, scale):
+    """Every rank of a config 3 / 4 run opens the model file rank 0 wrote:
+    the synthetic spec (and so the file name) must not depend on the rank's
+    own draw of prompt lengths, and its context covers every rank's."""
+    import types
+    sys.path.insert(0, ROOT)
+    import bench
+    args = types.SimpleNamespace(workload=workload, sessions=0, prompt_scale=scale)
+    for world in (2, 8):
+        plans = [bench.batched_plan(args, r, world) for r in range(world)]
+        paths = {bench.model_path(p[4]) for p in plans}
+        assert len(paths) == 1, paths
+        assert all(p[4].ctx >= p[3] for p in plans)
