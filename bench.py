@@ -6,7 +6,7 @@ random prompt, greedy decoding.  A "step" is one decode step: one token per
 session through all 32 layers, the LM head and the sampler.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c2|c3|c4|c5]
+                    [--workload c1|c2|c3|c4|c5|tok]
 
 Multi-GPU runs are launched with torch.distributed.run, one process per GPU;
 sessions are independent (weights replicated, no collective on the data
@@ -53,6 +53,10 @@ WORKLOADS["c3"] = dict(cfg=3, sessions=64, prompt=(16, 1024), gen=(32, 512), sam
 WORKLOADS["c4"] = dict(cfg=4, sessions=256, prompt=(32, 8192), gen=(256, 256), sample=False, log_prompt=True,
                       label="config4: SmolLM3-3B-shape, Q4_K + Q8_0 head, 256 concurrent sessions partitioned over "
                             "the GPUs, prompts log-uniform in [32,8192], 256 greedy decode tokens each")
+
+WORKLOADS["tok"] = dict(cfg=0, label="tokenizer encode: synthetic SentencePiece-style BPE vocabulary of 49152 tokens "
+                                     "(the SmolLM2 size), seeded random-word texts of 4000 characters (under the "
+                                     "reference's 4096-symbol cap per call), one host thread")
 
 GEMV_M, GEMV_K = 11008, 2048
 
@@ -417,12 +421,104 @@ def reference_gemv_rate(n_threads, reps):
     return n_threads * reps * blob.nbytes / max(times) / 1e9, max(times) / reps
 
 
+def tokenizer_setup():
+    """The vocabulary-only model file and the seeded texts of the tokenizer
+    workload."""
+    import numpy as np
+
+    from libcmol_b200 import synth
+    spec = synth.tiny_spec(synth.Q8_0, name="tokvocab", vocab_size=49152, n_layers=1, d_model=64, n_heads=2,
+                           n_kv_heads=1, d_ffn=128, ctx=256)
+    path = ensure_model(spec, 0, lambda: None)
+    rng = np.random.default_rng(1)
+    letters = list("abcdefghijklmnopqrstuvwxyz")
+    words = ["".join(rng.choice(letters, size=int(rng.integers(2, 9)))) for _ in range(2000)]
+    texts = []
+    for _ in range(16):
+        t = ""
+        while len(t) < 4000:
+            t += words[int(rng.integers(len(words)))] + " "
+        texts.append(t[:4000].encode())
+    return path, texts
+
+
+def reference_tokenizer_rate(path, texts):
+    """The reference's cmol_encode (oracle/_ref) over the texts, one thread:
+    (tokens/s, seconds, texts used)."""
+    from oracle.oracle import ReferenceModel
+    rm = ReferenceModel(path, 64)
+    try:
+        used = texts[:4]                      # ~0.5 s per 4000-character call
+        t0 = time.perf_counter()
+        ntok = sum(rm.encode(t.decode(), 8192)[0] for t in used)
+        sec = time.perf_counter() - t0
+    finally:
+        rm.close()
+    return ntok / sec, sec, len(used)
+
+
+def run_tokenizer(args, rank):
+    """Scope row f3 on the host: cmolcu_tokenizer_encode (heap-ordered merges)
+    against the reference's cmol_encode on the same vocabulary and texts."""
+    if rank != 0:
+        return
+    import ctypes as C
+
+    import numpy as np
+
+    from libcmol_b200 import lib
+    path, texts = tokenizer_setup()
+    L = lib()
+    L.cmolcu_tokenizer_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+    L.cmolcu_tokenizer_encode.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_int32), C.c_int]
+    L.cmolcu_tokenizer_free.argtypes = [C.c_void_p]
+    t = C.c_void_p()
+    if L.cmolcu_tokenizer_open(path.encode(), C.byref(t)) != 0:
+        raise RuntimeError("cmolcu_tokenizer_open failed")
+    out = np.zeros(8192, np.int32)
+    op = out.ctypes.data_as(C.POINTER(C.c_int32))
+    for x in texts[:args.warmup]:
+        L.cmolcu_tokenizer_encode(t, x, op, 8192)
+    reps = max(1, args.steps // len(texts))
+    t0 = time.perf_counter()
+    ntok = 0
+    for _ in range(reps):
+        for x in texts:
+            ntok += L.cmolcu_tokenizer_encode(t, x, op, 8192)
+    sec = time.perf_counter() - t0
+    L.cmolcu_tokenizer_free(t)
+    rate = ntok / sec
+    ref_rate, ref_sec, ref_n = reference_tokenizer_rate(path, texts)
+    print(json.dumps({
+        "metric": "tokenizer encode tokens/s (host CPU, one thread)", "value": round(rate, 1), "unit": "tokens/s",
+        "n_gpus": 0, "steps": reps * len(texts), "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3 / (reps * len(texts)), 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int32", "data": "synthetic", "config": {"workload": WORKLOADS["tok"]["label"]},
+        "cpu_baseline": {"value": round(ref_rate, 1), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                         "sample": f"{ref_n} texts of 4000 characters through the reference's cmol_encode "
+                                   f"({ref_sec:.2f} s)"},
+    }), flush=True)
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of the path on
     the host cores (see cpu_baseline)."""
     if rank != 0:
         return
     wl = WORKLOADS[args.workload]
+    if args.workload == "tok":
+        path, texts = tokenizer_setup()
+        rate, sec, n = reference_tokenizer_rate(path, texts)
+        print(json.dumps({
+            "impl": "reference", "metric": "tokenizer encode tokens/s (host CPU, one thread)", "value": round(rate, 1),
+            "unit": "tokens/s", "n_gpus": 0, "steps": n, "warmup": 0, "ms_per_step": round(sec * 1e3 / n, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+            "config": {"workload": wl["label"]},
+            "cpu_baseline": {"value": round(rate, 1), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                             "sample": f"{n} texts of 4000 characters through cmol_encode"},
+            "e2e": {"value": round(rate, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     if args.workload == "c5":
         cores = os.cpu_count() or 1
         gbs, sec = reference_gemv_rate(cores, max(4, args.steps // 4))
@@ -485,6 +581,11 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    if args.workload == "tok":
+        run_tokenizer(args, rank)
         if dist is not None:
             dist.destroy_process_group()
         return

@@ -11,6 +11,7 @@ import ctypes as C
 import json
 import os
 import re
+import sys
 
 import numpy as np
 import pytest
@@ -126,3 +127,33 @@ def test_tokenizer_merge_order_matches_reference_live(tmp_path):
         n = L.cmolcu_tokenizer_encode(t, text.encode(), out.ctypes.data_as(C.POINTER(C.c_int32)), 4096)
         assert n == n_ref and out[:max(n, 0)].tolist() == ids_ref.tolist(), text
     rm.close()
+
+
+def test_tokenizer_parity_on_bench_texts(tmp_path, monkeypatch):
+    """The tokenizer workload of bench.py (49152-token vocabulary, 4000-character
+    texts near the 4096-symbol cap) encodes to the reference's ids, and a text
+    past the cap gets the reference's answer too (needs the reference build)."""
+    from oracle.oracle import Reference, ReferenceModel
+    if not Reference.available():
+        pytest.skip("reference build (oracle/_ref) not present")
+    monkeypatch.setenv("CMOL_BENCH_CACHE", str(tmp_path))
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    from libcmol_b200 import lib
+    path, texts = bench.tokenizer_setup()
+    L = lib()
+    L.cmolcu_tokenizer_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+    L.cmolcu_tokenizer_encode.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_int32), C.c_int]
+    L.cmolcu_tokenizer_free.argtypes = [C.c_void_p]
+    t = C.c_void_p()
+    assert L.cmolcu_tokenizer_open(path.encode(), C.byref(t)) == 0
+    rm = ReferenceModel(path, 64)
+    try:
+        for text in texts[:2] + [texts[2] + texts[3][:1000]]:
+            n_ref, ids_ref = rm.encode(text.decode(), 8192)
+            out = np.zeros(8192, np.int32)
+            n = L.cmolcu_tokenizer_encode(t, text, out.ctypes.data_as(C.POINTER(C.c_int32)), 8192)
+            assert n == n_ref and out[:max(n, 0)].tolist() == ids_ref.tolist(), (len(text), n, n_ref)
+    finally:
+        rm.close()
+        L.cmolcu_tokenizer_free(t)
