@@ -312,6 +312,15 @@ orc_session_t *orc_session_new(const orc_model_t *m, int max_ctx) {
     return s;
 }
 
+/* Not part of the reference: an f16 KV format (the engine stores f32, as
+ * the reference does).  With orc_set_kv_f16(1) every K and V value is
+ * rounded to the nearest f16 (ties to even, the compiler's _Float16
+ * conversion) when written, so the effect of such a format on the logits
+ * can be measured against the f32 cache. */
+static int g_kv_f16 = 0;
+void orc_set_kv_f16(int on) { g_kv_f16 = on != 0; }
+static float kv_round_f16(float x) { return (float)(_Float16)x; }
+
 void orc_session_free(orc_session_t *s) {
     if (!s) return;
     free(s->k); free(s->v); free(s->scratch); free(s);
@@ -352,6 +361,11 @@ static void attn_forward(const orc_model_t *m, orc_session_t *s, int L, int pos,
     float *vl = s->v + (size_t)L * s->max_tokens * kvd;
     memcpy(kl + (size_t)pos * kvd, kb, (size_t)kvd * 4);
     memcpy(vl + (size_t)pos * kvd, vb, (size_t)kvd * 4);
+    if (g_kv_f16)                     /* study of an f16 KV format: store rounded */
+        for (int i = 0; i < kvd; i++) {
+            kl[(size_t)pos * kvd + i] = kv_round_f16(kb[i]);
+            vl[(size_t)pos * kvd + i] = kv_round_f16(vb[i]);
+        }
 
     float scale = 1.0f / sqrtf((float)hd);
     int   n     = pos + 1;

@@ -89,6 +89,8 @@ typedef struct orc_session orc_session_t;
 orc_session_t *orc_session_new(const orc_model_t *m, int max_ctx);
 void           orc_session_free(orc_session_t *s);
 void           orc_session_reset(orc_session_t *s);
+/* Study switch (not in the reference): store K and V rounded to f16. */
+void           orc_set_kv_f16(int on);
 int            orc_session_n_tokens(const orc_session_t *s);
 
 /* One token through the whole stack (src/model.c:176-276, src/attn.c:27-146).

@@ -93,6 +93,8 @@ class Oracle:
             L.orc_session_new.argtypes = [C.POINTER(OrcModel), C.c_int]
             L.orc_session_free.argtypes = [C.c_void_p]
             L.orc_session_reset.argtypes = [C.c_void_p]
+            L.orc_set_kv_f16.argtypes = [C.c_int]
+            L.orc_set_kv_f16.restype = None
             L.orc_session_n_tokens.argtypes = [C.c_void_p]
             L.orc_forward.restype = _fp
             L.orc_forward.argtypes = [C.POINTER(OrcModel), C.c_void_p, C.c_int32, C.c_int]

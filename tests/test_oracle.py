@@ -226,3 +226,37 @@ def test_golden_sampler():
         tok = L.orc_sample(fptr(lg), len(lg), p, st)
         assert tok == g["token"][i], i
         assert list(st) == [int(v) for v in g["rng_after"][i]], i
+
+
+@pytest.mark.parametrize("kw", [dict(dt=synth.Q8_0), dict(dt=synth.Q4_K, arch="smollm3", no_rope_interval=2,
+                                                          rope_base=5e6, qk_norm=True, tied=False, dt_head=8,
+                                                          n_heads=4, n_kv_heads=1, d_model=512)],
+                         ids=["q8_0", "smollm3-shape"])
+def test_f16_kv_cache_stays_within_logit_tolerance(tmp_path, kw):
+    """Groundwork for an f16 KV format (not in the reference, which stores
+    f32): the oracle with K and V rounded to f16 on write, against the f32
+    cache, over a 600-token context.  Every compared step must stay within
+    the engine's logit tolerance (max-abs 2e-2, cosine 0.9999)."""
+    kw = dict(kw)
+    dt = kw.pop("dt")
+    path = str(tmp_path / "kv.gguf")
+    synth.write_gguf(path, synth.tiny_spec(dt, ctx=1024, **kw))
+    om = OracleModel(path, lanes=16)
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, 512, size=600)
+    worst_abs, worst_cos = 0.0, 1.0
+    s32, s16 = om.session(1024), om.session(1024)
+    try:
+        for i, t in enumerate(toks):
+            om.L.orc_set_kv_f16(0)
+            a = om.forward(s32, int(t), i)
+            om.L.orc_set_kv_f16(1)
+            b = om.forward(s16, int(t), i)
+            worst_abs = max(worst_abs, float(np.abs(a - b).max()))
+            worst_cos = min(worst_cos, float(np.dot(a, b) / (np.linalg.norm(a) * np.linalg.norm(b))))
+    finally:
+        om.L.orc_set_kv_f16(0)
+        om.free_session(s32)
+        om.free_session(s16)
+    print(f"f16 KV over 600 tokens: max-abs {worst_abs:.3g}, min cosine {worst_cos:.9f}")
+    assert worst_abs <= 2e-2 and worst_cos >= 0.9999
