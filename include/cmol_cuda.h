@@ -73,6 +73,16 @@ cmol_err_t cmol_generate_batch(cmol_batch_item_t *items, int n_items);
  * [vocab] out (the analogue of cmol_model_forward, src/model.h:21-24). */
 cmol_err_t cmol_forward_logits(cmol_session_t *s, int32_t token, float *logits_out);
 
+/* Teacher forcing for n sessions in ONE decode step (n columns): session
+ * ss[i] runs tokens[i] at its next position and logits_out[i*vocab ..
+ * (i+1)*vocab) receives its logits.  The sessions must be distinct and on
+ * one GPU (cmol_session_device), n at most that GPU's step width (the
+ * model's max_sessions share plus its prefill chunk).  A step of 16 or more
+ * columns runs the tensor-core matmuls, so this is how a test checks the
+ * wide-batch path logit by logit. */
+cmol_err_t cmol_forward_logits_batch(cmol_session_t *const *ss, const int32_t *tokens, int n,
+                                     float *logits_out);
+
 int cmol_session_n_tokens(const cmol_session_t *s);
 int cmol_session_device(const cmol_session_t *s);
 int cmol_vocab_size(const cmol_model_t *m);
@@ -94,6 +104,13 @@ typedef struct {
     int       graph_steps;       /* steps run through a CUDA graph        */
     long long steps;             /* all steps (prefill, decode and mixed) */
     double    step_ms_total;     /* device time of all steps              */
+    unsigned  last_fault_code;   /* device fault word of the last failed
+                                    step (0: none since load): 1/2 GEMV
+                                    pipeline wait, 3 token id outside the
+                                    vocabulary, 4 page outside the pool,
+                                    5 sampler found no finite candidate,
+                                    6 attention page wait, 7 grid barrier
+                                    of the persistent step kernel       */
 } cmol_cuda_stats_t;
 
 cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats_t *out);
@@ -106,6 +123,30 @@ cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats
 cmol_err_t cmol_cuda_gemv_sweep(cmol_model_t *m, int gpu_index, int reps, double *ms_per_pass,
                                 long long *bytes_per_pass, int *launches_per_pass);
 void       cmol_cuda_stats_reset(cmol_model_t *m);
+
+/* One kernel class of the last step run on GPU `gpu_index`, replayed alone
+ * `reps` times from a CUDA graph; device milliseconds per pass (CUDA events
+ * on the engine stream), algorithmic bytes and flops per pass, launches per
+ * pass.  Must not overlap a generation on that GPU (CMOL_ERR_NO_SESSION).
+ *   CMOL_CUDA_SWEEP_MATMUL    : every weight product of the step at its
+ *                               width, no KV written; bytes = GGUF bytes of
+ *                               the matrices, flops = 2 * weights * columns;
+ *   CMOL_CUDA_SWEEP_ATTENTION : the step's attention over the same sessions
+ *                               and positions (reads the KV cache only);
+ *                               bytes = K and V bytes at those positions. */
+#define CMOL_CUDA_SWEEP_MATMUL 0
+#define CMOL_CUDA_SWEEP_ATTENTION 1
+cmol_err_t cmol_cuda_kernel_sweep(cmol_model_t *m, int gpu_index, int what, int reps, double *ms_per_pass,
+                                  long long *bytes_per_pass, double *flops_per_pass, int *launches_per_pass);
+
+/* Fault-path test hook.  The next decode step on GPU `gpu_index` carries a
+ * planted error that the kernels' own bounds checks catch, record in the
+ * device fault word and skip (no out-of-range access happens):
+ *   kind 1: column 0's token id is vocab + 3 (code 3);
+ *   kind 2: a page-table update names a page past the pool (code 4).
+ * That step fails: the requests in it return CMOL_ERR_INVALID, and
+ * cmol_cuda_stats reports the code.  Later steps run normally. */
+cmol_err_t cmol_cuda_debug_inject(cmol_model_t *m, int gpu_index, int kind);
 int        cmol_cuda_n_gpus(const cmol_model_t *m);
 
 #ifdef __cplusplus

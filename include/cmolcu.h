@@ -119,11 +119,14 @@ void cmolcu_matmul(float *out, const void *a, const float *b,
  * static device array of CMOLCU_NOALLOC_SCRATCH_BYTES per device:
  *   256 + up256(m * row_bytes(k)) + up256(repacked planes of A)
  *       + up256(4*k*n) + up256(4*m*n)       must be <= the limit
- * (up256 = round up to 256; e.g. 11008 x 2048 Q8_0 fits up to n = 128).
+ * (up256 = round up to 256; e.g. 11008 x 2048 Q8_0 fits up to n = 367).
  * Larger requests are rejected: out untouched, cmolcu_last_error() says so.
  * cmolcu_last_error() is "" after a call that succeeded.
  * The first call on each device looks up the scratch address and sets the
- * GEMV's shared-memory attribute; make it before any stream capture.
+ * GEMV's shared-memory attribute; make it before any stream capture.  The
+ * address is kept for the life of the process: do not call this again on a
+ * device after cudaDeviceReset.  The array is part of every CUDA context
+ * that loads libcmol.so, the decode engine's included. 
  * Calls on one device share the scratch: overlapping calls (two threads at
  * once) race and must be serialised by the caller. */
 #define CMOLCU_NOALLOC_SCRATCH_BYTES (64u << 20)

@@ -432,6 +432,7 @@ void Worker::run() {
     std::vector<PageUpdate> upd;
     std::vector<Request *> batch;
     std::vector<int32_t> out;
+    std::vector<float> logits;      // [columns][vocab] of a teacher-forcing step
     const int P = e->page_tokens();
     // A request belongs to the thread waiting in submit_and_wait, which may
     // return (and destroy it) as soon as finish() signals it: so a request is
@@ -493,19 +494,21 @@ void Worker::run() {
         active.swap(keep);
         if (active.empty()) continue;
 
-        // build the step: forward-only requests run alone
+        // build the step: forward-only (teacher-forcing) requests run
+        // together, in a step of their own
         cols.clear();
         upd.clear();
         batch.clear();
-        Request *fwd = nullptr;
+        bool fwd = false;
         for (Request *r : active)
-            if (r->forward_only) { fwd = r; break; }
+            if (r->forward_only) { fwd = true; break; }
         const int cap = e->max_batch();
         const int prefill = std::max(1, std::min(m->cfg.prefill_chunk, 256));
         struct Entry {
             Request *r;
             int n;        // columns of this request in the step
             int scol;     // the column whose sampled token it takes, or -1
+            int c0;       // its first column
         };
         std::vector<Entry> ent;
         // one column of request r at offset `off` past its next token; false
@@ -546,7 +549,7 @@ void Worker::run() {
         std::vector<Request *> order;
         int ncols = 0;
         for (Request *r : active) {
-            if (fwd && r != fwd) continue;
+            if (fwd && !r->forward_only) continue;
             if (ncols >= cap) break;
             order.push_back(r);
             want.push_back(1);
@@ -564,7 +567,7 @@ void Worker::run() {
         }
         for (size_t i = 0; i < order.size(); i++) {
             Request *r = order[i];
-            Entry en{r, 0, -1};
+            Entry en{r, 0, -1, (int)cols.size()};
             for (int k = 0; k < want[i]; k++) {
                 if (!add_col(r, k)) break;          // no KV page left: take fewer tokens
                 if (cols.back().sample) en.scol = (int)cols.size() - 1;
@@ -576,7 +579,11 @@ void Worker::run() {
         }
         if (batch.empty()) continue;
         out.assign(cols.size(), -1);
-        float *lg = fwd ? fwd->logits_out : nullptr;
+        float *lg = nullptr;
+        if (fwd) {
+            logits.resize(cols.size() * (size_t)m->vocab);
+            lg = logits.data();
+        }
         if (e->step(cols, upd, out.data(), lg) != 0) {
             logf(m, CMOL_LOG_ERROR, "decode step failed on GPU %d: %s", e->device(), e->last_error());
             for (Request *r : batch) retire(r, CMOL_ERR_INVALID);
@@ -589,7 +596,11 @@ void Worker::run() {
             s->n_tokens += en.n;
             const int np = (int)r->prompt.size();
             if (r->fed < np) r->fed += en.n;
-            if (r->forward_only) { retire(r, CMOL_OK); continue; }
+            if (r->forward_only) {
+                memcpy(r->logits_out, lg + (size_t)en.c0 * m->vocab, (size_t)m->vocab * sizeof(float));
+                retire(r, CMOL_OK);
+                continue;
+            }
             if (en.scol < 0) continue;
             const int32_t t = out[(size_t)en.scol];
             const int is_eos = (m->eos >= 0 && t == m->eos) ? 1 : 0;
@@ -716,6 +727,46 @@ extern "C" cmol_err_t cmol_forward_logits(cmol_session_t *s, int32_t token, floa
     return submit_and_wait(s, r, nullptr, nullptr, nullptr);
 }
 
+extern "C" cmol_err_t cmol_forward_logits_batch(cmol_session_t *const *ss, const int32_t *tokens, int n,
+                                                float *logits_out) {
+    if (!ss || !tokens || !logits_out || n <= 0 || !ss[0]) return CMOL_ERR_ARGS;
+    cmol_model_t *m = ss[0]->model;
+    const int gpu = ss[0]->gpu;
+    Worker *w = m->workers[(size_t)gpu].get();
+    if (n > w->eng->max_batch()) return CMOL_ERR_ARGS;
+    for (int i = 0; i < n; i++) {
+        if (!ss[i] || ss[i]->model != m || ss[i]->gpu != gpu) return CMOL_ERR_ARGS;
+        if (tokens[i] < 0 || tokens[i] >= m->vocab) return CMOL_ERR_ARGS;
+        if (ss[i]->n_tokens >= m->cfg.max_ctx) return CMOL_ERR_CTX_FULL;
+        for (int j = 0; j < i; j++)
+            if (ss[j] == ss[i]) return CMOL_ERR_ARGS;
+    }
+    std::vector<std::unique_ptr<Request>> rs;
+    rs.reserve((size_t)n);
+    for (int i = 0; i < n; i++) {
+        rs.emplace_back(new Request());
+        Request &r = *rs.back();
+        r.s = ss[i];
+        r.start_n = ss[i]->n_tokens;
+        r.prompt.assign(1, tokens[i]);
+        r.forward_only = true;
+        r.logits_out = logits_out + (size_t)i * m->vocab;
+    }
+    {
+        // one hand-over: the worker takes all of them into the same step
+        std::lock_guard<std::mutex> lk(w->mu);
+        for (auto &r : rs) w->incoming.push_back(r.get());
+    }
+    w->cv.notify_all();
+    cmol_err_t st = CMOL_OK;
+    for (auto &r : rs) {
+        std::unique_lock<std::mutex> lk(r->mu);
+        r->cv.wait(lk, [&] { return r->finished; });
+        if (r->status != CMOL_OK && st == CMOL_OK) st = r->status;
+    }
+    return st;
+}
+
 extern "C" cmol_err_t cmol_generate_batch(cmol_batch_item_t *items, int n) {
     if (!items || n <= 0) return CMOL_ERR_ARGS;
     std::vector<std::thread> th;
@@ -756,6 +807,29 @@ extern "C" cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int g, cmol_cuda_st
     out->graph_steps = (int)e->stats.graph_steps;
     out->steps = e->stats.steps;
     out->step_ms_total = e->stats.step_ms_total;
+    out->last_fault_code = e->last_fault();
+    return CMOL_OK;
+}
+
+extern "C" cmol_err_t cmol_cuda_kernel_sweep(cmol_model_t *m, int g, int what, int reps, double *ms_per_pass,
+                                             long long *bytes_per_pass, double *flops_per_pass,
+                                             int *launches_per_pass) {
+    if (!m || g < 0 || g >= (int)m->workers.size() || reps <= 0 || !ms_per_pass || !bytes_per_pass ||
+        !flops_per_pass || !launches_per_pass)
+        return CMOL_ERR_ARGS;
+    Worker *w = m->workers[(size_t)g].get();
+    std::lock_guard<std::mutex> lk(w->mu);
+    if (!w->active.empty() || !w->incoming.empty()) return CMOL_ERR_NO_SESSION;
+    if (w->eng->kernel_sweep(what, reps, ms_per_pass, bytes_per_pass, flops_per_pass, launches_per_pass)) {
+        logf(m, CMOL_LOG_ERROR, "%s", w->eng->last_error());
+        return CMOL_ERR_INVALID;
+    }
+    return CMOL_OK;
+}
+
+extern "C" cmol_err_t cmol_cuda_debug_inject(cmol_model_t *m, int g, int kind) {
+    if (!m || g < 0 || g >= (int)m->workers.size() || kind < 1 || kind > 2) return CMOL_ERR_ARGS;
+    m->workers[(size_t)g]->eng->inject_fault(kind);
     return CMOL_OK;
 }
 

@@ -390,6 +390,15 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
         wbytes += (long long)(ly.wo.q.bytes + ly.gu.q.bytes + ly.down.q.bytes);
     }
     e->weight_bytes_ = wbytes;
+    {
+        long long wv = (long long)V * D;   // the LM head (the embedding when tied)
+        for (const Layer &ly : d->layers) {
+            const DevWeight *ws[] = {&ly.qkv, &ly.q, &ly.k, &ly.v, &ly.wo, &ly.gu, &ly.down};
+            for (const DevWeight *w : ws)
+                if (w->base) wv += (long long)w->q.rows * w->q.k;
+        }
+        e->weight_values_ = wv;
+    }
     std::vector<uint8_t>().swap(buf);
 
     // ---- RoPE table: theta = pos / base^(2i/d_head), src/model.c:146-148 ----
@@ -551,9 +560,15 @@ static cudaError_t step_matmul(Engine::Impl *d, const GemvArgs &a, int ncol, int
     return gemv_launch_cols(a, ncol, epi, st, pdl);
 }
 
+// What record_step records: the whole step, only its weight products, or
+// only its attention launches (the last two for the kernel sweeps).
+enum { REC_FULL = 0, REC_MATMUL = 1, REC_ATTN = 2 };
+
 // Records the kernels of one step for `ncol` columns on the engine stream.
 static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol, int max_pages, int &launches,
-                               bool gemv_only = false, bool grouped = false) {
+                               int only = REC_FULL, bool grouped = false) {
+    const bool gemv_only = only == REC_MATMUL;
+    const bool mm = only != REC_ATTN;
     const HParams &hp = d->hp;
     const int D = hp.d_model, F = hp.d_ffn, V = hp.vocab_size;
     const int hd = hp.d_head, nkv = hp.n_kv_heads, KVD = nkv * hd;
@@ -573,7 +588,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
     sb.d_model = D;
     sb.fault = d->fault;
     const int dsi = ncol <= 1 ? 0 : ncol <= 2 ? 1 : ncol <= 4 ? 2 : -1;
-    if (!gemv_only && dsi >= 0 && d->ds_ok[dsi]) {
+    if (only == REC_FULL && dsi >= 0 && d->ds_ok[dsi]) {
         // one persistent kernel for all layers and the head, between the
         // step-begin kernel (which also zeroes its barrier counter) and the sampler
         sb.sync_reset = d->ds_sync;
@@ -610,7 +625,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         launches = 3;
         return cudaSuccess;
     }
-    if (!gemv_only) {
+    if (only == REC_FULL) {
         if ((e = step_begin_launch(sb, ncol, st, false)) != cudaSuccess) return e;
         launches++;
     }
@@ -644,14 +659,15 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             a.qkv.row_base = row_base;
             return step_matmul(d, a, ncol, EPI_QKV, st, pdl, launches);
         };
-        if (ly.fused_qkv) {
+        if (!mm) {
+        } else if (ly.fused_qkv) {
             if ((e = qkv_part(ly.qkv, 0)) != cudaSuccess) return e;
         } else {
             if ((e = qkv_part(ly.q, 0)) != cudaSuccess) return e;
             if ((e = qkv_part(ly.k, D)) != cudaSuccess) return e;
             if ((e = qkv_part(ly.v, D + KVD)) != cudaSuccess) return e;
         }
-        if (qkn && !gemv_only) {
+        if (qkn && only == REC_FULL) {
             QkNormArgs qa = {};
             qa.qkv = d->qkvbuf; qa.qkv_ld = D + 2 * KVD;
             qa.q_out = d->qbuf; qa.q_ld = D;
@@ -677,6 +693,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             if ((e = attention_launch(at, ncol, st, pdl)) != cudaSuccess) return e;
             launches++;
         }
+        if (!mm) continue;
         // --- output projection + residual -----------------------------------
         {
             GemvArgs a = g;
@@ -702,6 +719,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
             if ((e = step_matmul(d, a, ncol, EPI_RESID, st, pdl, launches)) != cudaSuccess) return e;
         }
     }
+    if (!mm) return cudaSuccess;
     // --- final norm + LM head, sampler ----------------------------------------
     {
         GemvArgs a = g;
@@ -761,6 +779,22 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         m[4 * B + 2 + 3 * u] = upd[u].index;
         m[4 * B + 3 + 3 * u] = upd[u].page;
     }
+    // planted errors of the fault-path tests: both are caught by the bounds
+    // checks of k_step_begin, which record the code and skip the access
+    const int inject = inject_.exchange(0);
+    if (inject == 1) {
+        m[0] = vocab_ + 3;
+    } else if (inject == 2 && (int)upd.size() < B) {
+        const int u = (int)upd.size();
+        m[4 * B] = u + 1;
+        m[4 * B + 1 + 3 * u] = cols[0].slot;
+        m[4 * B + 2 + 3 * u] = 0;
+        m[4 * B + 3 + 3 * u] = n_pages_ + 5;
+    }
+    last_meta_.assign(m, m + d->meta_ints);
+    last_n_ = n;
+    last_bucket_ = bucket;
+    last_grouped_ = grouped;
     cudaError_t e = cudaMemcpyAsync(d->meta_dev, d->meta_host, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice,
                                     d->stream);
     if (e == cudaSuccess) e = cudaEventRecord(d->ev0, d->stream);
@@ -770,7 +804,7 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         if (!opt_.use_graphs || it == d->graphs.end()) {
             // eager launches: always the first step of a bucket (sets kernel
             // attributes outside any capture), every step without graphs
-            e = record_step(d, opt_, bucket, max_pages_, launches, false, grouped);
+            e = record_step(d, opt_, bucket, max_pages_, launches, REC_FULL, grouped);
             d->launches = launches;
             if (e == cudaSuccess && opt_.use_graphs) {
                 // capture this bucket for the next steps (capture does not run)
@@ -779,7 +813,7 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
                 int l2 = 0;
                 e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
                 if (e == cudaSuccess) {
-                    cudaError_t re = record_step(d, opt_, bucket, max_pages_, l2, false, grouped);
+                    cudaError_t re = record_step(d, opt_, bucket, max_pages_, l2, REC_FULL, grouped);
                     e = cudaStreamEndCapture(d->stream, &g);
                     if (re != cudaSuccess) e = re;
                 }
@@ -803,6 +837,7 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
     }
     const unsigned int fault = (unsigned int)d->out_host[B];
     if (fault) {
+        last_fault_ = fault;
         cudaMemsetAsync(d->fault, 0, sizeof(unsigned int), d->stream);
         // an abandoned step can leave attention split counters behind
         cudaMemsetAsync(d->counters, 0, (size_t)B * d->hp.n_kv_heads * sizeof(int), d->stream);
@@ -863,11 +898,11 @@ int Engine::gemv_sweep(int reps, double *ms_per_pass, long long *bytes_per_pass,
     cudaGraphExec_t ge = nullptr;
     cudaError_t e = cudaMemcpyAsync(d->meta_dev, d->meta_host, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice,
                                     d->stream);
-    if (e == cudaSuccess) e = record_step(d, opt_, 1, max_pages_, launches, true);   // eager warm-up
+    if (e == cudaSuccess) e = record_step(d, opt_, 1, max_pages_, launches, REC_MATMUL);   // eager warm-up
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
     if (e == cudaSuccess) e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
     if (e == cudaSuccess) {
-        cudaError_t re = record_step(d, opt_, 1, max_pages_, launches, true);
+        cudaError_t re = record_step(d, opt_, 1, max_pages_, launches, REC_MATMUL);
         e = cudaStreamEndCapture(d->stream, &g);
         if (re != cudaSuccess) e = re;
     }
@@ -887,6 +922,77 @@ int Engine::gemv_sweep(int reps, double *ms_per_pass, long long *bytes_per_pass,
     }
     *ms_per_pass = (double)ms / reps;
     *bytes_per_pass = weight_bytes_;
+    *launches_per_pass = launches;
+    return 0;
+}
+
+int Engine::kernel_sweep(int what, int reps, double *ms_per_pass, long long *bytes_per_pass, double *flops_per_pass,
+                         int *launches_per_pass) {
+    if (last_n_ <= 0 || (what != 0 && what != 1) || reps <= 0) {
+        snprintf(err_, sizeof err_, "kernel_sweep: no step has run yet, or bad arguments");
+        return -1;
+    }
+    cudaSetDevice(device_);
+    const int B = opt_.max_batch;
+    int *m = d->meta_host;
+    memcpy(m, last_meta_.data(), d->meta_ints * sizeof(int));
+    m[4 * B] = 0;                                    // no page-table updates
+    long long bytes = 0;
+    double flops = 0.0;
+    const HParams &hp = d->hp;
+    if (what == 0) {
+        for (int i = 0; i < B; i++) m[B + i] = -1;   // inactive: the products run, no KV is written
+        bytes = weight_bytes_;
+        flops = 2.0 * (double)weight_values_ * last_n_;
+    } else {
+        for (int i = 0; i < last_n_; i++) {
+            const int pos = last_meta_[(size_t)B + i];
+            if (pos < 0) continue;
+            bytes += (long long)(pos + 1) * kv_bytes_per_token_;
+            flops += 4.0 * hp.n_heads * hp.d_head * (pos + 1) * hp.n_layers;
+        }
+    }
+    const int only = what == 0 ? REC_MATMUL : REC_ATTN;
+    int launches = 0;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t e = cudaMemcpyAsync(d->meta_dev, m, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice, d->stream);
+    if (e == cudaSuccess) e = record_step(d, opt_, last_bucket_, max_pages_, launches, only, last_grouped_);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        cudaError_t re = record_step(d, opt_, last_bucket_, max_pages_, launches, only, last_grouped_);
+        e = cudaStreamEndCapture(d->stream, &g);
+        if (re != cudaSuccess) e = re;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
+    if (e == cudaSuccess) e = cudaGraphLaunch(ge, d->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev0, d->stream);
+    for (int r = 0; e == cudaSuccess && r < reps; r++) e = cudaGraphLaunch(ge, d->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev1, d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, d->ev0, d->ev1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    // restore the last step's metadata on the device
+    if (e == cudaSuccess) {
+        memcpy(m, last_meta_.data(), d->meta_ints * sizeof(int));
+        e = cudaMemcpyAsync(d->meta_dev, m, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice, d->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    }
+    if (e != cudaSuccess) {
+        snprintf(err_, sizeof err_, "kernel_sweep: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    const unsigned int fault = fault_code();
+    if (fault) {
+        snprintf(err_, sizeof err_, "kernel_sweep: device fault code %u", fault);
+        return -1;
+    }
+    *ms_per_pass = (double)ms / reps;
+    *bytes_per_pass = bytes;
+    *flops_per_pass = flops;
     *launches_per_pass = launches;
     return 0;
 }

@@ -9,6 +9,7 @@
 #pragma once
 #include <stdint.h>
 
+#include <atomic>
 #include <vector>
 
 #include "host_model.h"
@@ -87,7 +88,24 @@ class Engine {
     // (graph, CUDA events); bytes = GGUF bytes of all matrices streamed.
     int gemv_sweep(int reps, double *ms_per_pass, long long *bytes_per_pass, int *launches_per_pass);
 
+    // One kernel class of the LAST step, replayed alone `reps` times from a
+    // CUDA graph (device time per pass by CUDA events on the engine stream):
+    //   what 0: its weight products at its width (columns marked inactive,
+    //           so no KV is written); bytes = GGUF bytes of every matrix,
+    //           flops = 2 * weights * live columns;
+    //   what 1: its attention launches over the same sessions, positions and
+    //           pages (read-only on the KV cache); bytes = the K and V bytes
+    //           those positions read, flops = 4 * heads * d_head * tokens.
+    int kernel_sweep(int what, int reps, double *ms_per_pass, long long *bytes_per_pass, double *flops_per_pass,
+                     int *launches_per_pass);
+
     const char *last_error() const { return err_; }
+    // Fault-path test hook: the next step carries a planted error that the
+    // device checks catch and skip (1: column 0's token id past the
+    // vocabulary; 2: a page-table update naming a page outside the pool).
+    void inject_fault(int kind) { inject_.store(kind); }
+    // Device fault code of the last failed step (0 = none since load).
+    unsigned int last_fault() const { return last_fault_; }
     EngineStats stats;
     void reset_stats() { stats = EngineStats(); }
     unsigned int fault_code();   // device fault word (0 = none); clears it
@@ -101,6 +119,12 @@ class Engine {
     EngineOptions opt_;
     int n_pages_ = 0, max_pages_ = 0, vocab_ = 0;
     long long weight_bytes_ = 0, kv_bytes_per_token_ = 0;
+    std::atomic<int> inject_{0};
+    std::vector<int> last_meta_;      // step metadata of the last step (host copy)
+    int last_n_ = 0, last_bucket_ = 0;
+    bool last_grouped_ = false;
+    long long weight_values_ = 0;     // weights of every matrix one step streams
+    unsigned int last_fault_ = 0;
     char err_[256] = {0};
     friend struct EngineBuilder;
 };

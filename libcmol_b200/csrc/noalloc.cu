@@ -27,11 +27,17 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[CMOLCU_NOALLOC_
 
 // Address of g_noalloc_scratch on each device, resolved once per device with
 // that device current (the host never passes the symbol itself to a kernel).
+// The cache lives as long as the process: after a cudaDeviceReset the module
+// may be loaded at another address, so a process that resets a device must
+// not call this entry point on it again.
 static unsigned char *g_scratch_ptr[64];
 static std::mutex g_scratch_mu;
 
 static unsigned char *scratch_for(int dev) {
-    if (dev < 0 || dev >= 64) return nullptr;
+    if (dev < 0 || dev >= 64) {
+        cmolcu_set_error("cmolcu_matmul_noalloc: device %d is above the 64-device table", dev);
+        return nullptr;
+    }
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (!g_scratch_ptr[dev]) {
         void *p = nullptr;

@@ -58,7 +58,8 @@ class CudaStats(C.Structure):
                 ("prefill_tokens", C.c_longlong), ("decode_ms", C.c_double),
                 ("step_ms_last", C.c_double), ("weight_bytes", C.c_longlong),
                 ("kv_bytes_read", C.c_longlong), ("kernel_launches_per_step", C.c_int),
-                ("graph_steps", C.c_int), ("steps", C.c_longlong), ("step_ms_total", C.c_double)]
+                ("graph_steps", C.c_int), ("steps", C.c_longlong), ("step_ms_total", C.c_double),
+                ("last_fault_code", C.c_uint)]
 
 
 class BatchItem(C.Structure):
@@ -99,6 +100,10 @@ def api():
     sig("cmol_generate_ids", C.c_int, [_vp, _ip, C.c_int, C.POINTER(GenParams), ID_CB, _vp])
     sig("cmol_generate_batch", C.c_int, [C.POINTER(BatchItem), C.c_int])
     sig("cmol_forward_logits", C.c_int, [_vp, C.c_int32, _fp])
+    sig("cmol_forward_logits_batch", C.c_int, [C.POINTER(_vp), _ip, C.c_int, _fp])
+    sig("cmol_cuda_debug_inject", C.c_int, [_vp, C.c_int, C.c_int])
+    sig("cmol_cuda_kernel_sweep", C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
+                                            C.POINTER(C.c_longlong), C.POINTER(C.c_double), C.POINTER(C.c_int)])
     sig("cmol_session_n_tokens", C.c_int, [_vp])
     sig("cmol_session_device", C.c_int, [_vp])
     sig("cmol_vocab_size", C.c_int, [_vp])
@@ -172,6 +177,29 @@ class Model:
         _chk(api().cmol_cuda_gemv_sweep(self.h, gpu, reps, C.byref(ms), C.byref(nb), C.byref(nl)),
              "cmol_cuda_gemv_sweep")
         return ms.value, nb.value, nl.value
+
+    def kernel_sweep(self, what: int, gpu: int = 0, reps: int = 10):
+        """cmol_cuda_kernel_sweep of the last step: what 0 = weight products,
+        1 = attention.  Returns (ms, bytes, flops, launches) per pass."""
+        ms, nb, fl, nl = C.c_double(0), C.c_longlong(0), C.c_double(0), C.c_int(0)
+        _chk(api().cmol_cuda_kernel_sweep(self.h, gpu, what, reps, C.byref(ms), C.byref(nb), C.byref(fl),
+                                          C.byref(nl)), "cmol_cuda_kernel_sweep")
+        return ms.value, nb.value, fl.value, nl.value
+
+    def forward_logits_batch(self, sessions, tokens) -> np.ndarray:
+        """cmol_forward_logits_batch: one step, one column per session;
+        returns the logits [n][vocab]."""
+        n = len(sessions)
+        hs = (_vp * n)(*[s.h for s in sessions])
+        toks = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros((n, self.vocab), np.float32)
+        _chk(api().cmol_forward_logits_batch(hs, toks.ctypes.data_as(_ip), n, out.ctypes.data_as(_fp)),
+             "cmol_forward_logits_batch")
+        return out
+
+    def debug_inject(self, kind: int, gpu: int = 0):
+        """cmol_cuda_debug_inject: plant a caught error in the next step."""
+        _chk(api().cmol_cuda_debug_inject(self.h, gpu, kind), "cmol_cuda_debug_inject")
 
     def encode(self, text: str, cap: int = 4096):
         out = np.zeros(cap, np.int32)

@@ -129,10 +129,47 @@ print("ok")
 
 
 @pytest.mark.gpu
-def test_wide_batch_uses_tensor_cores(gpu, golden, paths):
-    """Sixteen sessions in one step take the tensor-core path (default
-    threshold); every session decodes to the requested length, and the
-    greedy streams agree with the reference up to f16 rounding (reported)."""
+@pytest.mark.parametrize("name", ["q4_k", "smollm3", "mixed", "q8_0"])
+def test_wide_batch_uses_tensor_cores(gpu, paths, name):
+    """32 sessions, each on its own random token sequence, advance together
+    one token a step (32 columns: the tensor-core products at the default
+    threshold).  Every column's logits are checked against the C
+    restatement run on that session alone: max-abs <= 2e-2 and cosine >=
+    0.9999, the engine's specified tolerance."""
+    from libcmol_b200.model import Model
+    from oracle.oracle import OracleModel
+    NS, T = 32, 12
+    rng = np.random.default_rng(21)
+    seqs = rng.integers(0, 512, size=(NS, T)).astype(np.int32)
+    om = OracleModel(paths[name], lanes=16)
+    oss = [om.session(64) for _ in range(NS)]
+    with Model(paths[name], max_ctx=64, max_sessions=NS) as m:
+        ss = [m.acquire() for _ in range(NS)]
+        worst, wcos = 0.0, 1.0
+        for t in range(T):
+            lg = m.forward_logits_batch(ss, seqs[:, t])
+            for i in range(NS):
+                ref = om.forward(oss[i], int(seqs[i, t]), t)
+                d, c = float(np.abs(lg[i] - ref).max()), _cos(lg[i], ref)
+                worst, wcos = max(worst, d), min(wcos, c)
+                assert d <= ATOL and c >= COS, (t, i, d, c)
+        print(f"{name}: 32-column steps, worst max-abs {worst:.2e} cos {wcos:.7f}")
+        for s in ss:
+            assert s.n_tokens == T
+            s.release()
+    for o in oss:
+        om.free_session(o)
+
+
+@pytest.mark.gpu
+def test_wide_batch_generate(gpu, golden, paths):
+    """Sixteen sessions generated together through cmol_generate_batch (their
+    steps widen to the tensor-core threshold as the requests arrive): every
+    stream has the requested length and starts with the reference's token;
+    how many equal the reference's f32 stream throughout is reported, since
+    a greedy decision within f16 rounding may differ.  The per-column
+    numerics of wide steps are checked logit by logit in
+    test_wide_batch_uses_tensor_cores."""
     from libcmol_b200.model import GenParams, Model
     name = "q4_k"
     with Model(paths[name], max_ctx=64, max_sessions=16) as m:
@@ -141,10 +178,9 @@ def test_wide_batch_uses_tensor_cores(gpu, golden, paths):
         p = GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=20)
         outs = m.generate_batch(ss, [prompt] * 16, [p] * 16)
         ref = golden[f"{name}_gen_greedy"].tolist()
-        assert all(len(o) == len(ref) for o in outs)
+        assert all(len(o) == len(ref) and o[0] == ref[0] for o in outs)
         same = sum(o.tolist() == ref for o in outs)
         print(f"wide batch: {same}/16 streams identical to the reference")
-        assert all(o[0] == ref[0] for o in outs)
         st = m.stats(0)
         assert st.kernel_launches_per_step > 0
         for s in ss:
