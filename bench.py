@@ -50,9 +50,14 @@ WORKLOADS["c3"] = dict(cfg=3, sessions=64, prompt=(16, 1024), gen=(32, 512), sam
                       label="config3: SmolLM2-1.7B-shape, Q5_0 attention / Q4_K FFN, 64 concurrent sessions per GPU, "
                             "prompts uniform in [16,1024], generations uniform in [32,512], top-p 0.9 with a "
                             "per-session seed, continuous batching")
+WORKLOADS["c4job"] = dict(cfg=4, sessions=256, prompt=(32, 8192), gen=(256, 256), sample=False, log_prompt=True,
+                         label="config4 whole job: SmolLM3-3B-shape, Q4_K + Q8_0 head, 256 concurrent sessions "
+                               "partitioned over the GPUs, prompts log-uniform in [32,8192], 256 greedy decode "
+                               "tokens each, prefill included")
 WORKLOADS["c4"] = dict(cfg=4, sessions=256, prompt=(32, 8192), gen=(256, 256), sample=False, log_prompt=True,
-                      label="config4: SmolLM3-3B-shape, Q4_K + Q8_0 head, 256 concurrent sessions partitioned over "
-                            "the GPUs, prompts log-uniform in [32,8192], 256 greedy decode tokens each")
+                      label="config4: SmolLM3-3B-shape, Q4_K + Q8_0 head, 256 concurrent ragged sessions partitioned "
+                            "over the GPUs (prompts log-uniform in [32,8192]), greedy continuous-batching decode: "
+                            "every step one token for every session")
 
 WORKLOADS["tok"] = dict(cfg=0, label="tokenizer encode: synthetic SentencePiece-style BPE vocabulary of 49152 tokens "
                                      "(the SmolLM2 size), seeded random-word texts of 4000 characters (under the "
@@ -151,6 +156,147 @@ def run_batched(args, rank, world, local, barrier, dist=None):
         "clocks": clocks.summary(),
         "peak_source": peak_kind,
     }), flush=True)
+
+
+def kv_format_name(kv):
+    return {0: "f32", 1: "f16"}.get(kv, str(kv))
+
+
+def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
+    """Config 4, the north-star aggregate: 256 ragged sessions partitioned
+    over the GPUs (strong scaling), every session prefilled with its own
+    prompt (log-uniform in [32, 8192]) before the timed region; then W
+    warm-up and K timed decode steps, each one token for every session of
+    the GPU (cmol_generate_batch, continuous batching).
+    value = sessions of all ranks * K / max over ranks of the device time of
+    those K steps (CUDA events around every step on the engine stream);
+    e2e = the same tokens over the wall time of the timed cmol_generate_batch
+    call (host buffers; every step copies its ids and positions in and the
+    sampled ids out)."""
+    import numpy as np
+
+    from libcmol_b200.model import GenParams, Model
+    wl = WORKLOADS["c4"]
+    K, W = args.steps, args.warmup
+    sessions, plen, _, _, spec, rng = batched_plan(args, rank, world)
+    path = ensure_model(spec, rank, barrier)
+    V = spec.vocab_size
+    prompts = [rng.integers(0, V, int(n)).astype(np.int32) for n in plen]
+    ctx = int(plen.max()) + W + K + 8
+    greedy = lambda k: GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=k)   # noqa: E731
+    t_load = time.perf_counter()
+    with Model(path, max_ctx=ctx, max_sessions=sessions, devices=[local], kv_dtype=args.kv) as m:
+        t_load = time.perf_counter() - t_load
+        ss = [m.acquire() for _ in range(sessions)]
+        # untimed: prefill of every prompt (batched, one sampled token each), then W decode steps
+        m.reset_stats()
+        t_pf = time.perf_counter()
+        outs = m.generate_batch(ss, prompts, [greedy(1)] * sessions)
+        t_pf = time.perf_counter() - t_pf
+        st = m.stats(0)
+        prefill_ms, prefill_steps = st.step_ms_total, st.steps
+        last = [int(o[-1]) for o in outs]
+        outs = m.generate_batch(ss, [[t] for t in last], [greedy(W)] * sessions)
+        last = [int(o[-1]) for o in outs]
+        ctx_now = [s.n_tokens for s in ss]
+        clocks = Clocks(local)
+        clocks.start()
+        barrier()
+        m.reset_stats()
+        t0 = time.perf_counter()
+        outs = m.generate_batch(ss, [[t] for t in last], [greedy(K)] * sessions)
+        t1 = time.perf_counter()
+        barrier()
+        clocks.stop()
+        assert all(len(o) == K for o in outs), [len(o) for o in outs]
+        st = m.stats(0)
+        dev_ms, steps, wall_ms = st.decode_ms, st.decode_steps, (t1 - t0) * 1000.0
+        launches = st.kernel_launches_per_step
+        assert st.decode_tokens == sessions * K, (st.decode_tokens, sessions * K)
+        # the kernel classes of the last step, replayed alone (outside the timed region)
+        attn = m.kernel_sweep(1, reps=5)
+        mm = m.kernel_sweep(0, reps=5)
+        for s in ss:
+            s.release()
+    (tok_all, ses_all, ctx_sum), (dev_ms, wall_ms, steps_max) = reduce_ranks(
+        dist, f"cuda:{local}", sums=(sessions * K, sessions, sum(ctx_now)), maxes=(dev_ms, wall_ms, steps))
+    nested = None
+    if world == 1 and not args.no_nested:
+        nested = run_single(args, rank, world, local, barrier, dist, "c2", steps=max(20, min(K, 256)),
+                            with_cpu=False)
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
+    tc_peak = tensor_peak()
+    a_gbs = attn[1] / (attn[0] * 1e-3) / 1e9
+    m_tfs = mm[2] / (mm[0] * 1e-3) / 1e12
+    m_gbs = mm[1] / (mm[0] * 1e-3) / 1e9
+    kernels = {
+        "attention": {"ms_per_step": round(attn[0], 4), "launches": attn[3], "kv_bytes": attn[1],
+                      "GBps": round(a_gbs, 1), "frac_hbm": round(a_gbs / hbm, 4)},
+        "matmul": {"ms_per_step": round(mm[0], 4), "launches": mm[3], "weight_bytes": mm[1],
+                   "TFLOPs": round(m_tfs, 1), "frac_tensor": round(m_tfs / tc_peak, 4), "GBps": round(m_gbs, 1)},
+    }
+    if attn[0] >= mm[0]:
+        roof = {"bound": "hbm", "achieved": round(a_gbs, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(a_gbs / hbm, 4), "traffic": traffic_of("attention_c4"),
+                "kernel": "attention (all layers of one decode step, graph replay)",
+                "bytes_per_launch": int(attn[1] // max(1, attn[3])),
+                "launch_us": round(1000.0 * attn[0] / max(1, attn[3]), 3), "peak_source": peak_kind}
+    else:
+        roof = {"bound": "tensor", "achieved": round(m_tfs, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                "frac": round(m_tfs / tc_peak, 4), "traffic": traffic_of("matmul_c4"),
+                "kernel": "tensor-core weight products (all of one decode step, graph replay)",
+                "launch_us": round(1000.0 * mm[0] / max(1, mm[3]), 3), "peak_source": "measured bf16 burst"}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(args, wl)
+        except Exception as ex:      # the checker is test infrastructure; report, do not fail
+            cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"unavailable: {ex}"}
+    line = {
+        "metric": "decode tokens/sec (aggregate over GPUs)", "value": round(tok_all / (dev_ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (f16 tensor-core products)", "data": "synthetic",
+        "config": {"workload": wl["label"], "model": spec.name, "sessions": int(ses_all),
+                   "sessions_per_gpu": sessions, "kv_cache": kv_format_name(args.kv),
+                   "mean_context_timed": round(ctx_sum / max(1, ses_all) + K / 2, 1),
+                   "decode_steps_timed": int(steps_max),
+                   "l2": "each step reads every weight and every session's KV (GBs), far above the 126 MB L2"},
+        "e2e": {"value": round(tok_all / (wall_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * (7 * sessions + 1), "d2h_bytes_per_step": 4 * (sessions + 1)},
+        "roofline": roof,
+        "kernels": kernels,
+        "cpu_baseline": cpu,
+        "gpu_launches": int(steps_max * launches),
+        "clocks": clocks.summary(),
+        "untimed": {"model_load_s": round(t_load, 1), "prefill_s": round(t_pf, 1),
+                    "prefill_tokens": int(plen.sum()), "prefill_steps": int(prefill_steps),
+                    "prefill_device_ms": round(prefill_ms, 1)},
+        "single_session_config2": None if not nested else
+            {k: nested[k] for k in ("value", "unit", "ms_per_step", "e2e", "roofline", "config") if k in nested},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def traffic_of(key):
+    """DRAM bytes per launch of a kernel from an ncu capture committed under
+    profiles/traffic.json (null when there is none)."""
+    prof = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        return json.load(open(prof)).get(key)
+    except (OSError, ValueError):
+        return None
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(p))["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0
 
 
 def run_gemv_microbench(args, rank, local):
@@ -546,15 +692,121 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
+def run_single(args, rank, world, local, barrier, dist, workload, steps=None, with_cpu=True):
+    """Configs 1 and 2: one session per GPU (weak scaling), K timed decode
+    steps after a prefill of the prompt and W warm-up steps.  Returns the
+    JSON line on rank 0 (None elsewhere)."""
+    import numpy as np
+
+    from libcmol_b200 import synth
+    from libcmol_b200.model import GenParams, Model
+
+    K = steps or args.steps
+    wl = dict(WORKLOADS[workload])
+    if args.prompt > 0:
+        wl["prompt"] = args.prompt
+        wl["label"] += f" (prompt overridden to {args.prompt} tokens)"
+    spec = synth.baseline_spec(wl["cfg"])
+    path = ensure_model(spec, rank, barrier)
+    ctx = wl["prompt"] + args.warmup + K + 8
+    rng = np.random.default_rng(1000 + rank)
+    prompt = rng.integers(0, spec.vocab_size, size=wl["prompt"]).tolist()
+
+    with Model(path, max_ctx=ctx, max_sessions=1, devices=[local]) as m:
+        s = m.acquire()
+        # warm-up: prefill + W decode steps (graphs captured, clocks up)
+        rc, ids = s.generate_ids(prompt, GenParams.make(0.0, max_new_tokens=args.warmup))
+        assert rc == 0 and len(ids) == args.warmup, (rc, ids)
+        last = ids[-1]
+        clocks = Clocks(local)
+        clocks.start()
+        barrier()
+        m.reset_stats()
+        t0 = time.perf_counter()
+        # K timed decode steps: the first forwards the last warm-up token
+        rc, ids = s.generate_ids([last], GenParams.make(0.0, max_new_tokens=K))
+        t1 = time.perf_counter()
+        barrier()
+        clocks.stop()
+        assert rc == 0 and len(ids) == K, (rc, len(ids))
+        st = m.stats(0)
+        dev_ms = st.decode_ms
+        wall_ms = (t1 - t0) * 1000.0
+        launches = st.kernel_launches_per_step
+        # the dominant kernel, measured live outside the timed region
+        sweep_ms, sweep_bytes, sweep_launches = m.gemv_sweep(0, reps=20)
+        s.release()
+
+    _, (dev_ms, wall_ms) = reduce_ranks(dist, f"cuda:{local}", maxes=(dev_ms, wall_ms))
+
+    if rank == 0:
+        n = world
+        tokens = n * K
+        value = tokens / (dev_ms / 1000.0)
+        e2e = tokens / (wall_ms / 1000.0)
+        peak, peak_kind = peaks()
+        achieved = sweep_bytes / (sweep_ms / 1000.0) / 1e9
+        traffic = None
+        prof = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(prof):
+            try:
+                traffic = json.load(open(prof)).get(spec.name)
+            except ValueError:
+                traffic = None
+        cpu = None
+        if n == 1 and with_cpu and not args.no_cpu_baseline:
+            try:
+                cpu = cpu_baseline(args, wl)
+            except Exception as ex:      # the checker is test infrastructure; report, do not fail
+                cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                       "sample": f"unavailable: {ex}"}
+        line = {
+            "metric": "decode tokens/sec (aggregate over GPUs)",
+            "value": round(value, 2),
+            "unit": "tokens/s",
+            "n_gpus": n,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / K, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": wl["label"], "model": spec.name, "sessions_per_gpu": 1,
+                       "prompt_tokens": wl["prompt"], "decode_tokens_timed": K,
+                       "weights_bytes_per_step": sweep_bytes,
+                       "l2": "weights streamed per step exceed the 126 MB L2 (no flush needed)"
+                             if sweep_bytes > 126e6 else "weights fit in L2: steady state, not flushed"},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * (4 * 1 + 1 + 3),
+                    "d2h_bytes_per_step": 4 * 2},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "k_gemv (all GEMV launches of one decode step, graph replay)",
+                         "peak_source": peak_kind,
+                         "bytes_per_launch": int(sweep_bytes // max(1, sweep_launches)),
+                         "launch_us": round(1000.0 * sweep_ms / max(1, sweep_launches), 3)},
+            "cpu_baseline": cpu,
+            "gpu_launches": int(K * launches),
+            "clocks": clocks.summary(),
+        }
+        return line
+    return None
+
+
 def main():
     import faulthandler
     faulthandler.enable()          # a native crash prints the Python frames that led to it
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS))
+    ap.add_argument("--kv", type=int, default=1,
+                    help="KV cache format of config 4: 0 = f32 (the reference's), 1 = f16 (default; logits "
+                         "within the 2e-2 / 0.9999 parity tolerance, tests/test_kv_f16_gpu.py)")
+    ap.add_argument("--no-nested", action="store_true", help="skip the nested config-2 single-session line")
     ap.add_argument("--ref-steps", type=int, default=24)
     ap.add_argument("--ref-prompt", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -594,108 +846,17 @@ def main():
         if dist is not None:
             dist.destroy_process_group()
         return
-    if args.workload in ("c3", "c4"):
+    if args.workload in ("c3", "c4job"):
         run_batched(args, rank, world, local, barrier, dist)
-        if dist is not None:
-            dist.destroy_process_group()
-        return
-
-    import numpy as np
-
-    from libcmol_b200 import synth
-    from libcmol_b200.model import GenParams, Model
-
-    wl = dict(WORKLOADS[args.workload])
-    if args.prompt > 0:
-        wl["prompt"] = args.prompt
-        wl["label"] += f" (prompt overridden to {args.prompt} tokens)"
-    spec = synth.baseline_spec(wl["cfg"])
-    path = ensure_model(spec, rank, barrier)
-    ctx = wl["prompt"] + args.warmup + args.steps + 8
-    rng = np.random.default_rng(1000 + rank)
-    prompt = rng.integers(0, spec.vocab_size, size=wl["prompt"]).tolist()
-
-    with Model(path, max_ctx=ctx, max_sessions=1, devices=[local]) as m:
-        s = m.acquire()
-        # warm-up: prefill + W decode steps (graphs captured, clocks up)
-        rc, ids = s.generate_ids(prompt, GenParams.make(0.0, max_new_tokens=args.warmup))
-        assert rc == 0 and len(ids) == args.warmup, (rc, ids)
-        last = ids[-1]
-        clocks = Clocks(local)
-        clocks.start()
-        barrier()
-        m.reset_stats()
-        t0 = time.perf_counter()
-        # K timed decode steps: the first forwards the last warm-up token
-        rc, ids = s.generate_ids([last], GenParams.make(0.0, max_new_tokens=args.steps))
-        t1 = time.perf_counter()
-        barrier()
-        clocks.stop()
-        assert rc == 0 and len(ids) == args.steps, (rc, len(ids))
-        st = m.stats(0)
-        dev_ms = st.decode_ms
-        wall_ms = (t1 - t0) * 1000.0
-        launches = st.kernel_launches_per_step
-        # the dominant kernel, measured live outside the timed region
-        sweep_ms, sweep_bytes, sweep_launches = m.gemv_sweep(0, reps=20)
-        s.release()
-
-    _, (dev_ms, wall_ms) = reduce_ranks(dist, f"cuda:{local}", maxes=(dev_ms, wall_ms))
-
-    if rank == 0:
-        n = world
-        tokens = n * args.steps
-        value = tokens / (dev_ms / 1000.0)
-        e2e = tokens / (wall_ms / 1000.0)
-        peak, peak_kind = peaks()
-        achieved = sweep_bytes / (sweep_ms / 1000.0) / 1e9
-        traffic = None
-        prof = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(prof):
-            try:
-                traffic = json.load(open(prof)).get(spec.name)
-            except ValueError:
-                traffic = None
-        cpu = None
-        if n == 1 and not args.no_cpu_baseline:
-            try:
-                cpu = cpu_baseline(args, wl)
-            except Exception as ex:      # the checker is test infrastructure; report, do not fail
-                cpu = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
-                       "sample": f"unavailable: {ex}"}
-        line = {
-            "metric": "decode tokens/sec (aggregate over GPUs)",
-            "value": round(value, 2),
-            "unit": "tokens/s",
-            "n_gpus": n,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(dev_ms / args.steps, 4),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": wl["label"], "model": spec.name, "sessions_per_gpu": 1,
-                       "prompt_tokens": wl["prompt"], "decode_tokens_timed": args.steps,
-                       "weights_bytes_per_step": sweep_bytes,
-                       "l2": "weights streamed per step exceed the 126 MB L2 (no flush needed)"
-                             if sweep_bytes > 126e6 else "weights fit in L2: steady state, not flushed"},
-            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * (4 * 1 + 1 + 3),
-                    "d2h_bytes_per_step": 4 * 2},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "k_gemv (all GEMV launches of one decode step, graph replay)",
-                         "peak_source": peak_kind,
-                         "bytes_per_launch": int(sweep_bytes // max(1, sweep_launches)),
-                         "launch_us": round(1000.0 * sweep_ms / max(1, sweep_launches), 3)},
-            "cpu_baseline": cpu,
-            "gpu_launches": int(args.steps * launches),
-            "clocks": clocks.summary(),
-        }
-        print(json.dumps(line), flush=True)
+    elif args.workload == "c4":
+        run_decode_aggregate(args, rank, world, local, barrier, dist)
+    else:
+        line = run_single(args, rank, world, local, barrier, dist, args.workload)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
+
 
 
 if __name__ == "__main__":

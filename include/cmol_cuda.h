@@ -29,12 +29,18 @@ cmol_err_t cmol_cuda_set_devices(const int *devices, int n);
  *                    (default 0.85)
  *   max_batch      : most sessions in one decode step (default max_sessions)
  *   use_graphs     : 1 = capture the decode step in a CUDA graph (default),
- *                    0 = launch kernels directly (debugging)            */
+ *                    0 = launch kernels directly (debugging)
+ *   kv_dtype       : KV cache format, 0 = f32 (the reference's own,
+ *                    src/cmol_internal.h:142-147; default), 1 = f16 (every
+ *                    K and V value rounded to the nearest f16 when written:
+ *                    half the KV memory and attention traffic; logits stay
+ *                    within the engine's 2e-2 / cosine 0.9999 tolerance) */
 typedef struct {
     int   kv_page_tokens;
     float kv_pool_frac;
     int   max_batch;
     int   use_graphs;
+    int   kv_dtype;
 } cmol_cuda_options_t;
 void cmol_cuda_set_options(const cmol_cuda_options_t *opt);
 
@@ -109,8 +115,7 @@ typedef struct {
                                     pipeline wait, 3 token id outside the
                                     vocabulary, 4 page outside the pool,
                                     5 sampler found no finite candidate,
-                                    6 attention page wait, 7 grid barrier
-                                    of the persistent step kernel       */
+                                    6 attention page wait               */
 } cmol_cuda_stats_t;
 
 cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats_t *out);
@@ -124,7 +129,8 @@ cmol_err_t cmol_cuda_gemv_sweep(cmol_model_t *m, int gpu_index, int reps, double
                                 long long *bytes_per_pass, int *launches_per_pass);
 void       cmol_cuda_stats_reset(cmol_model_t *m);
 
-/* One kernel class of the last step run on GPU `gpu_index`, replayed alone
+/* One kernel class of the widest step run on GPU `gpu_index` since load or
+ * the last cmol_cuda_stats_reset (the latest of equal width), replayed alone
  * `reps` times from a CUDA graph; device milliseconds per pass (CUDA events
  * on the engine stream), algorithmic bytes and flops per pass, launches per
  * pass.  Must not overlap a generation on that GPU (CMOL_ERR_NO_SESSION).

@@ -117,7 +117,7 @@ struct cmol_model {
 // ---------------------------------------------------------------------------
 static std::mutex g_cfg_mu;
 static std::vector<int> g_devices;
-static cmol_cuda_options_t g_opts = {0, 0.f, 0, 1};
+static cmol_cuda_options_t g_opts = {0, 0.f, 0, 1, 0};
 
 static void logf(const cmol_model_t *m, int level, const char *fmt, ...) {
     if (!m || !m->cfg.log_fn) return;
@@ -139,7 +139,7 @@ extern "C" cmol_err_t cmol_cuda_set_devices(const int *devices, int n) {
 extern "C" void cmol_cuda_set_options(const cmol_cuda_options_t *opt) {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     if (opt) g_opts = *opt;
-    else g_opts = cmol_cuda_options_t{0, 0.f, 0, 1};
+    else g_opts = cmol_cuda_options_t{0, 0.f, 0, 1, 0};
 }
 
 static std::vector<int> pick_devices() {
@@ -234,6 +234,11 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
         std::lock_guard<std::mutex> lk(g_cfg_mu);
         opt = g_opts;
     }
+    if (opt.kv_dtype != 0 && opt.kv_dtype != 1) {
+        cmol_free(m);
+        if (err) *err = CMOL_ERR_ARGS;
+        return nullptr;
+    }
     std::vector<int> devs = pick_devices();
     const int ng = (int)devs.size();
     std::vector<int> errs((size_t)ng, 0);
@@ -257,6 +262,7 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
             eo.page_tokens = opt.kv_page_tokens > 0 ? opt.kv_page_tokens : 16;
             eo.kv_pool_frac = opt.kv_pool_frac > 0.f ? opt.kv_pool_frac : 0.85f;
             eo.use_graphs = opt.use_graphs != 0;
+            eo.kv_f16 = opt.kv_dtype == 1;
             eo.split_tokens = 64;
             if (eo.split_tokens % eo.page_tokens) eo.split_tokens = eo.page_tokens * 4;
             char msg[256] = {0};

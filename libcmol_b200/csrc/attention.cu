@@ -7,8 +7,8 @@
 
 #include <algorithm>
 
-size_t attention_smem_bytes(int d_head, int G, int split_tokens, int q_chunk) {
-    return attn_group_smem_bytes(d_head, G, split_tokens, q_chunk) + 16;   // + the mbarrier
+size_t attention_smem_bytes(int d_head, int G, int split_tokens, int q_chunk, int kvb) {
+    return attn_group_smem_bytes(d_head, G, split_tokens, q_chunk, kvb) + 16;   // + the mbarrier
 }
 
 int attention_q_chunk(int d_head, int G, int split_tokens) {
@@ -20,11 +20,12 @@ int attention_q_chunk(int d_head, int G, int split_tokens) {
 
 // Steps without prefill groups: one CTA per (split, kv head, column), each
 // running attn_item.
-template <int E>
+template <int E, bool H>
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a) {
     const int G = a.n_heads / a.n_kv;
     float *sm = reinterpret_cast<float *>(cmolcu_smem);
-    uint64_t *bar = reinterpret_cast<uint64_t *>(cmolcu_smem + attn_item_smem_bytes(32 * E, G, a.split_tokens));
+    uint64_t *bar =
+        reinterpret_cast<uint64_t *>(cmolcu_smem + attn_item_smem_bytes(32 * E, G, a.split_tokens, H ? 2 : 4));
     __shared__ AttnShared sh;
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
@@ -37,8 +38,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a) {
     const int col = blockIdx.z;
     const int pos = a.pos[col];
     const int srow = a.slot ? a.slot[col] : col;
-    attn_item<E>(a, blockIdx.x, blockIdx.y, col, pos, a.page_table + (long long)srow * a.max_pages, sm, bar, parity,
-                 sh, threadIdx.x);
+    attn_item<E, H>(a, blockIdx.x, blockIdx.y, col, pos, a.page_table + (long long)srow * a.max_pages, sm, bar,
+                    parity, sh, threadIdx.x);
 }
 
 // Steps with prefill groups: one CTA per (split, kv head, column).  A column
@@ -46,12 +47,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(AttnArgs a) {
 // group are served by their block leaders (attn_group_item).  CTAs per SM
 // that the shared memory of the engine's shapes allows (d_head 64: 5, 128:
 // 3); registers are held to that.
-template <int E>
+template <int E, bool H>
 __global__ void __launch_bounds__(ATTN_THREADS, E <= 2 ? 5 : E == 4 ? 3 : 2) k_attn_group(AttnArgs a) {
     const int G = a.n_heads / a.n_kv;
     float *sm = reinterpret_cast<float *>(cmolcu_smem);
-    uint64_t *bar =
-        reinterpret_cast<uint64_t *>(cmolcu_smem + attn_group_smem_bytes(32 * E, G, a.split_tokens, a.q_chunk));
+    uint64_t *bar = reinterpret_cast<uint64_t *>(
+        cmolcu_smem + attn_group_smem_bytes(32 * E, G, a.split_tokens, a.q_chunk, H ? 2 : 4));
     __shared__ union {
         AttnShared      one;
         AttnGroupShared grp;
@@ -74,10 +75,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, E <= 2 ? 5 : E == 4 ? 3 : 2) k_a
     const bool prev = grouped && cp != c && slot_p == slot && pos_p == pos - 1;
     const bool next = grouped && cn != c && slot_n == slot && pos_n == pos + 1;
     if (pos >= 0 && (prev || next))
-        attn_group_item<E>(a, blockIdx.x, blockIdx.y, c, pos, slot, next, sm, bar, parity, sh.grp, threadIdx.x);
+        attn_group_item<E, H>(a, blockIdx.x, blockIdx.y, c, pos, slot, next, sm, bar, parity, sh.grp, threadIdx.x);
     else
-        attn_item<E>(a, blockIdx.x, blockIdx.y, c, pos, a.page_table + (long long)slot * a.max_pages, sm, bar, parity,
-                     sh.one, threadIdx.x);
+        attn_item<E, H>(a, blockIdx.x, blockIdx.y, c, pos, a.page_table + (long long)slot * a.max_pages, sm, bar,
+                        parity, sh.one, threadIdx.x);
 }
 
 // Work-list launch (opt-in): a fixed grid of a few CTAs per SM; each
@@ -89,11 +90,12 @@ __global__ void __launch_bounds__(ATTN_THREADS, E <= 2 ? 5 : E == 4 ? 3 : 2) k_a
 // do not have.
 #define ATTN_LIST_MAX_COLS 1024
 
-template <int E>
+template <int E, bool H>
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn_list(AttnArgs a, int ncol) {
     const int G = a.n_heads / a.n_kv;
     float *sm = reinterpret_cast<float *>(cmolcu_smem);
-    uint64_t *bar = reinterpret_cast<uint64_t *>(cmolcu_smem + attn_item_smem_bytes(32 * E, G, a.split_tokens));
+    uint64_t *bar =
+        reinterpret_cast<uint64_t *>(cmolcu_smem + attn_item_smem_bytes(32 * E, G, a.split_tokens, H ? 2 : 4));
     __shared__ AttnShared sh;
     __shared__ int start[ATTN_LIST_MAX_COLS + 1];   // start[c] = first item of column c
     __shared__ int wsum[ATTN_WARPS];
@@ -145,22 +147,26 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_list(AttnArgs a, int ncol
         const int hk = r / nsp, sp = r % nsp;
         const int pos = a.pos[col];
         const int srow = a.slot ? a.slot[col] : col;
-        if (!attn_item<E>(a, sp, hk, col, pos, a.page_table + (long long)srow * a.max_pages, sm, bar, parity, sh, tid))
+        if (!attn_item<E, H>(a, sp, hk, col, pos, a.page_table + (long long)srow * a.max_pages, sm, bar, parity, sh,
+                             tid))
             return;   // fault recorded (uniform over the CTA)
     }
 }
 
-template <int E>
+template <int E, bool H>
 static cudaError_t launch_e(const AttnArgs &a, int ncol, size_t smem, cudaStream_t st, bool pdl) {
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {   // per process: the B200s of one box share the limit
-        cudaError_t e = cudaFuncSetAttribute(k_attn<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_attn<E, H>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_attn_group<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
+            e = cudaFuncSetAttribute(k_attn_group<E, H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     CMOLCU_ATTN_SMEM_MAX);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_attn_list<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, CMOLCU_ATTN_SMEM_MAX);
+            e = cudaFuncSetAttribute(k_attn_list<E, H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     CMOLCU_ATTN_SMEM_MAX);
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
@@ -177,10 +183,10 @@ static cudaError_t launch_e(const AttnArgs &a, int ncol, size_t smem, cudaStream
     }();
     const bool list = force_list;
     if (list && ncol <= ATTN_LIST_MAX_COLS)   // per-column items (no prefill groups)
-        return launch_k(k_attn_list<E>, dim3(sms * per_sm), dim3(ATTN_THREADS), smem, st, pdl, a, ncol);
+        return launch_k(k_attn_list<E, H>, dim3(sms * per_sm), dim3(ATTN_THREADS), smem, st, pdl, a, ncol);
     if (a.grouped)
-        return launch_k(k_attn_group<E>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
-    return launch_k(k_attn<E>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
+        return launch_k(k_attn_group<E, H>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
+    return launch_k(k_attn<E, H>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
 }
 
 cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl) {
@@ -189,14 +195,17 @@ cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool 
     if (a.split_tokens % a.page_tokens != 0 || a.n_splits < 1) return cudaErrorInvalidValue;
     if (a.q_chunk < 1 || a.q_chunk > ATTN_QB || a.q_block < 1 || a.q_block > ATTN_QB) return cudaErrorInvalidValue;
     // the group layout (a superset of the one-query layout) bounds both kernels
-    if (attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk) > CMOLCU_ATTN_SMEM_MAX) return cudaErrorInvalidValue;
-    const size_t smem = a.grouped ? attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk)
-                                  : attn_item_smem_bytes(a.d_head, G, a.split_tokens) + 16;
+    const int kvb = a.kv_f16 ? 2 : 4;
+    if (attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk, kvb) > CMOLCU_ATTN_SMEM_MAX)
+        return cudaErrorInvalidValue;
+    const size_t smem = a.grouped ? attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk, kvb)
+                                  : attn_item_smem_bytes(a.d_head, G, a.split_tokens, kvb) + 16;
+    const bool h = a.kv_f16 != 0;
     switch (a.d_head) {
-    case 64:  return launch_e<2>(a, ncol, smem, st, pdl);
-    case 128: return launch_e<4>(a, ncol, smem, st, pdl);
-    case 32:  return launch_e<1>(a, ncol, smem, st, pdl);
-    case 256: return launch_e<8>(a, ncol, smem, st, pdl);
+    case 64:  return h ? launch_e<2, true>(a, ncol, smem, st, pdl) : launch_e<2, false>(a, ncol, smem, st, pdl);
+    case 128: return h ? launch_e<4, true>(a, ncol, smem, st, pdl) : launch_e<4, false>(a, ncol, smem, st, pdl);
+    case 32:  return h ? launch_e<1, true>(a, ncol, smem, st, pdl) : launch_e<1, false>(a, ncol, smem, st, pdl);
+    case 256: return h ? launch_e<8, true>(a, ncol, smem, st, pdl) : launch_e<8, false>(a, ncol, smem, st, pdl);
     default: return cudaErrorInvalidValue;
     }
 }

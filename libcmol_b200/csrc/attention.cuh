@@ -22,9 +22,10 @@ struct AttnArgs {
     const int   *slot;       // [ncol] -> page-table row
     const int   *page_table; // [slots][max_pages]
     int          max_pages;
-    const float *kv_pages;
-    long long    page_floats;
+    const void  *kv_pages;       // f32 values, or f16 when kv_f16
+    long long    page_elems;     // K/V values per page
     int          n_pages;        // pages in the pool (bounds check)
+    int          kv_f16;         // 1: the pool holds f16 values
     unsigned int *fault;         // device fault word
     int          layer, n_heads, n_kv, d_head, page_tokens;
     int          split_tokens;   // multiple of page_tokens
@@ -42,9 +43,9 @@ inline size_t attn_part_floats(int ncol, int n_heads, int n_splits, int d_head) 
     return (size_t)ncol * n_heads * n_splits * (d_head + 2);
 }
 
-// Dynamic shared memory one CTA needs (K and V tiles, queries, scores) with
-// q_chunk queries per chunk.
-size_t attention_smem_bytes(int d_head, int group, int split_tokens, int q_chunk);
+// Dynamic shared memory one CTA needs (K and V tiles of kvb-byte values,
+// queries, scores) with q_chunk queries per chunk.
+size_t attention_smem_bytes(int d_head, int group, int split_tokens, int q_chunk, int kvb);
 // Queries per chunk for engines whose steps carry prefill groups: about 6 KB
 // of query and score tiles (decode-only engines use 1).
 int attention_q_chunk(int d_head, int group, int split_tokens);

@@ -1,6 +1,5 @@
-// attention_item.cuh — one work item of split-context GQA decode attention,
-// shared by the standalone kernel (attention.cu) and the persistent decode
-// step kernel (decode_step.cu).
+// attention_item.cuh — one work item of split-context GQA decode attention
+// (the kernels of attention.cu run it).
 //
 // Item = (context split s, kv head hk, column col), run by ATTN_THREADS
 // threads that synchronise on named barrier 1.  Thread 0 moves the K and V
@@ -30,10 +29,25 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Shared-memory floats of one item (K and V tiles, queries, scores, P.V sums).
-__host__ __device__ inline size_t attn_item_smem_bytes(int d_head, int G, int split_tokens) {
-    return (size_t)2 * split_tokens * d_head * 4 + (size_t)G * d_head * 4 + (size_t)G * split_tokens * 4 +
+// Shared-memory bytes of one item (K and V tiles of kvb-byte values,
+// queries, scores, P.V sums).
+__host__ __device__ inline size_t attn_item_smem_bytes(int d_head, int G, int split_tokens, int kvb) {
+    return (size_t)2 * split_tokens * d_head * kvb + (size_t)G * d_head * 4 + (size_t)G * split_tokens * 4 +
            (size_t)ATTN_THREADS * 16;
+}
+
+// Four consecutive K or V values (value index 4 * i4) of a shared-memory
+// tile as floats: f32 tiles directly, f16 tiles widened exactly.
+template <bool H>
+__device__ __forceinline__ float4 kv4(const unsigned char *tile, size_t i4) {
+    if constexpr (H) {
+        const uint2 u = reinterpret_cast<const uint2 *>(tile)[i4];
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+        return make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+        return reinterpret_cast<const float4 *>(tile)[i4];
+    }
 }
 
 // `sm` is 16-byte aligned; `bar` an initialised mbarrier (count 1) whose
@@ -41,21 +55,23 @@ __host__ __device__ inline size_t attn_item_smem_bytes(int d_head, int G, int sp
 // Returns false when a wait ran out (fault word set); every thread returns
 // the same value at the same point.
 // `pos` is the column's position (< 0: inactive) and `pt` its page-table row
-// (global or shared memory).
-template <int E>
+// (global or shared memory).  H: the KV pool holds f16 values.
+template <int E, bool H>
 __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, const int *pt, float *sm,
                           uint64_t *bar, uint32_t &parity, AttnShared &sh, int tid) {
     constexpr int hd = 32 * E, HD4 = hd / 4;
+    constexpr int KB = H ? 2 : 4;                // bytes per K / V value
     const int lane = tid & 31, warp = tid >> 5;
     const int G = a.n_heads / a.n_kv;
     const int S = a.split_tokens;
     const int P = a.page_tokens;
 
-    float *Ks = sm;                              // [S][hd]
-    float *Vs = Ks + (size_t)S * hd;             // [S][hd]
-    float *Qs = Vs + (size_t)S * hd;             // [G][hd]
-    float *Sc = Qs + (size_t)G * hd;             // [G][S]
-    float4 *Red = reinterpret_cast<float4 *>(Sc + (size_t)G * S);   // [ATTN_THREADS]
+    unsigned char *Ks = reinterpret_cast<unsigned char *>(sm);                 // [S][hd] values
+    unsigned char *Vs = Ks + (size_t)S * hd * KB;                                // [S][hd] values
+    float *Qs = reinterpret_cast<float *>(Vs + (size_t)S * hd * KB);             // [G][hd]
+    float *Sc = Qs + (size_t)G * hd;                                            // [G][S]
+    float4 *Red = reinterpret_cast<float4 *>(Sc + (size_t)G * S);               // [ATTN_THREADS]
+    const unsigned char *pool = static_cast<const unsigned char *>(a.kv_pages);
 
     if (pos < 0) return true;
     const int t0 = s * S;
@@ -75,11 +91,11 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
         if (ok) {
             // the KV rows of this step were written through the generic proxy
             fence_proxy_async_global();
-            mbar_arrive_expect_tx(bar, (uint32_t)(2 * npg * P * hd * 4));
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * npg * P * hd * KB));
             for (int i = 0; i < npg; i++) {
-                const float *kp = a.kv_pages + (long long)pt[t0 / P + i] * a.page_floats + head_off;
-                bulk_g2s(Ks + (size_t)i * P * hd, kp, (uint32_t)(P * hd * 4), bar);
-                bulk_g2s(Vs + (size_t)i * P * hd, kp + v_off, (uint32_t)(P * hd * 4), bar);
+                const unsigned char *kp = pool + ((long long)pt[t0 / P + i] * a.page_elems + head_off) * KB;
+                bulk_g2s(Ks + (size_t)i * P * hd * KB, kp, (uint32_t)(P * hd * KB), bar);
+                bulk_g2s(Vs + (size_t)i * P * hd * KB, kp + v_off * KB, (uint32_t)(P * hd * KB), bar);
             }
         } else if (a.fault) {
             atomicExch(a.fault, FAULT_BAD_PAGE);
@@ -101,17 +117,15 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
     // row at float4 l % HD4, so the 8 lanes of a shared-memory phase touch 8
     // different 16-byte bank groups of their (different) K rows.
     {
-        const float4 *K4 = reinterpret_cast<const float4 *>(Ks);
         const float4 *Q4 = reinterpret_cast<const float4 *>(Qs);
         for (int w = tid; w < n * G; w += ATTN_THREADS) {
             const int t = w % n, g = w / n;
-            const float4 *kr = K4 + (size_t)t * HD4;
             const float4 *qr = Q4 + (size_t)g * HD4;
             float d0 = 0.f, d1 = 0.f;
 #pragma unroll
             for (int j = 0; j < HD4; j++) {
                 const int c = (j + lane) & (HD4 - 1);
-                const float4 k = kr[c], q = qr[c];
+                const float4 k = kv4<H>(Ks, (size_t)t * HD4 + c), q = qr[c];
                 d0 = __fmaf_rn(q.x, k.x, d0);
                 d1 = __fmaf_rn(q.y, k.y, d1);
                 d0 = __fmaf_rn(q.z, k.z, d0);
@@ -148,10 +162,9 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                 const int g = it / HD4, c = it % HD4;
                 const float *p = Sc + g * S;
-                const float4 *V4 = reinterpret_cast<const float4 *>(Vs) + c;
                 for (int t = 0; t < n; t++) {
                     const float pt_ = p[t];
-                    const float4 v = V4[(size_t)t * HD4];
+                    const float4 v = kv4<H>(Vs, (size_t)t * HD4 + c);
                     acc.x = __fmaf_rn(pt_, v.x, acc.x);
                     acc.y = __fmaf_rn(pt_, v.y, acc.y);
                     acc.z = __fmaf_rn(pt_, v.z, acc.z);
@@ -168,11 +181,10 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             const int g = item / HD4, c = item % HD4;
             const float *p = Sc + g * S;
-            const float4 *V4 = reinterpret_cast<const float4 *>(Vs) + c;
             const int tb = (int)((long long)n * part / parts), te = (int)((long long)n * (part + 1) / parts);
             for (int t = tb; t < te; t++) {
                 const float pt_ = p[t];
-                const float4 v = V4[(size_t)t * HD4];
+                const float4 v = kv4<H>(Vs, (size_t)t * HD4 + c);
                 acc.x = __fmaf_rn(pt_, v.x, acc.x);
                 acc.y = __fmaf_rn(pt_, v.y, acc.y);
                 acc.z = __fmaf_rn(pt_, v.z, acc.z);
@@ -251,10 +263,10 @@ __host__ __device__ inline int attn_group_qc(int d_head, int G, int split_tokens
 
 // K and V tiles, query and score tiles, P.V sums, per-row max / sum and
 // per-query merge flags (floats, 16-byte multiple).
-__host__ __device__ inline size_t attn_group_smem_bytes(int d_head, int G, int split_tokens, int qc) {
+__host__ __device__ inline size_t attn_group_smem_bytes(int d_head, int G, int split_tokens, int qc, int kvb) {
     const size_t tail = ((size_t)2 * qc * G * 4 + (size_t)qc * 4 + 15) & ~(size_t)15;
-    return (size_t)2 * split_tokens * d_head * 4 + (size_t)qc * G * d_head * 4 + (size_t)qc * G * split_tokens * 4 +
-           (size_t)ATTN_THREADS * 16 + tail;
+    return (size_t)2 * split_tokens * d_head * kvb + (size_t)qc * G * d_head * 4 +
+           (size_t)qc * G * split_tokens * 4 + (size_t)ATTN_THREADS * 16 + tail;
 }
 
 struct AttnGroupShared {
@@ -264,10 +276,11 @@ struct AttnGroupShared {
 // Column c (position pos_c >= 0, page-table row slot_c) belongs to a group
 // of more than one column; `next` says whether column c + 1 continues it.
 // a.slot is non-null.
-template <int E>
+template <int E, bool H>
 __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos_c, int slot_c, bool next, float *sm,
                                 uint64_t *bar, uint32_t &parity, AttnGroupShared &gs, int tid) {
     constexpr int hd = 32 * E, HD4 = hd / 4;
+    constexpr int KB = H ? 2 : 4;                // bytes per K / V value
     const int lane = tid & 31, warp = tid >> 5;
     const int G = a.n_heads / a.n_kv;
     const int S = a.split_tokens;
@@ -281,9 +294,10 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
     if (t0 > pos_c) return true;
     const int n = min(S, pos_c + 1 - t0);                     // tokens of this split the block sees
 
-    float *Ks = sm;                                           // [S][hd]
-    float *Vs = Ks + (size_t)S * hd;                          // [S][hd]
-    float *Qs = Vs + (size_t)S * hd;                          // [QC][G][hd]
+    unsigned char *Ks = reinterpret_cast<unsigned char *>(sm);  // [S][hd] values
+    unsigned char *Vs = Ks + (size_t)S * hd * KB;               // [S][hd] values
+    float *Qs = reinterpret_cast<float *>(Vs + (size_t)S * hd * KB);   // [QC][G][hd]
+    const unsigned char *pool = static_cast<const unsigned char *>(a.kv_pages);
     float *Sc = Qs + (size_t)QC * G * hd;                     // [QC][G][S]
     float4 *Red = reinterpret_cast<float4 *>(Sc + (size_t)QC * G * S);   // [ATTN_THREADS]
     float *Wmax = reinterpret_cast<float *>(Red + ATTN_THREADS);         // [QC][G]
@@ -302,11 +316,11 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
         }
         if (ok) {
             fence_proxy_async_global();   // the KV rows of this step were written through the generic proxy
-            mbar_arrive_expect_tx(bar, (uint32_t)(2 * npg * P * hd * 4));
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * npg * P * hd * KB));
             for (int i = 0; i < npg; i++) {
-                const float *kp = a.kv_pages + (long long)pt[t0 / P + i] * a.page_floats + head_off;
-                bulk_g2s(Ks + (size_t)i * P * hd, kp, (uint32_t)(P * hd * 4), bar);
-                bulk_g2s(Vs + (size_t)i * P * hd, kp + v_off, (uint32_t)(P * hd * 4), bar);
+                const unsigned char *kp = pool + ((long long)pt[t0 / P + i] * a.page_elems + head_off) * KB;
+                bulk_g2s(Ks + (size_t)i * P * hd * KB, kp, (uint32_t)(P * hd * KB), bar);
+                bulk_g2s(Vs + (size_t)i * P * hd * KB, kp + v_off * KB, (uint32_t)(P * hd * KB), bar);
             }
         } else if (a.fault) {
             atomicExch(a.fault, FAULT_BAD_PAGE);
@@ -352,20 +366,18 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
         // position are masked.  Lane l starts its walk over the row at float4
         // l % HD4 (distinct bank groups across the lanes of a phase).
         {
-            const float4 *K4 = reinterpret_cast<const float4 *>(Ks);
             const float4 *Q4 = reinterpret_cast<const float4 *>(Qs);
             for (int w = tid; w < rows * n; w += ATTN_THREADS) {
                 const int t = w % n, row = w / n, qi = row / G;
                 const int nq = min(n, pos_c - (c - (qb + qi)) + 1 - t0);   // consecutive positions
                 float sc = -INFINITY;
                 if (t < nq) {
-                    const float4 *kr = K4 + (size_t)t * HD4;
                     const float4 *qr = Q4 + (size_t)row * HD4;
                     float d0 = 0.f, d1 = 0.f;
 #pragma unroll
                     for (int j = 0; j < HD4; j++) {
                         const int cc = (j + lane) & (HD4 - 1);
-                        const float4 k = kr[cc], q = qr[cc];
+                        const float4 k = kv4<H>(Ks, (size_t)t * HD4 + cc), q = qr[cc];
                         d0 = __fmaf_rn(q.x, k.x, d0);
                         d1 = __fmaf_rn(q.y, k.y, d1);
                         d0 = __fmaf_rn(q.z, k.z, d0);
@@ -408,11 +420,10 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
             auto pv = [&](int it, int tb, int te) {
                 const int row = it / HD4, cc = it % HD4;
                 const float *p = Sc + row * S;
-                const float4 *V4 = reinterpret_cast<const float4 *>(Vs) + cc;
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int t = tb; t < te; t++) {
                     const float pt_ = p[t];
-                    const float4 v = V4[(size_t)t * HD4];
+                    const float4 v = kv4<H>(Vs, (size_t)t * HD4 + cc);
                     acc.x = __fmaf_rn(pt_, v.x, acc.x);
                     acc.y = __fmaf_rn(pt_, v.y, acc.y);
                     acc.z = __fmaf_rn(pt_, v.z, acc.z);

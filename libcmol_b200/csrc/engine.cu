@@ -10,7 +10,6 @@
 #include <string>
 
 #include "attention.cuh"
-#include "decode_step.cuh"
 #include "gemm_tc.cuh"
 #include "gemv_launch.cuh"
 #include "step_kernels.cuh"
@@ -42,8 +41,8 @@ struct Engine::Impl {
     DevWeight           embd, head;       // head.base == nullptr when tied
     float              *out_norm = nullptr;
     float2             *rope_cs = nullptr;
-    float              *kv_pages = nullptr;
-    long long           page_floats = 0;
+    void               *kv_pages = nullptr;   // f32 or f16 values (EngineOptions::kv_f16)
+    long long           page_elems = 0;       // K/V values per page
     int                *page_table = nullptr;
     SlotSampler        *slots = nullptr;
     // step metadata: device block and pinned mirror (same layout)
@@ -66,21 +65,10 @@ struct Engine::Impl {
     std::map<int, cudaGraphExec_t> graphs;
     std::vector<void *> allocs;
     int launches = 0;
-    // persistent decode-step kernel (decode_step.cuh): phase table + plans for 1, 2, 4 columns
-    DsPhase      *ds_phases = nullptr;
-    int           ds_nphases = 0;
-    unsigned int *ds_sync = nullptr;
-    DsPlan        ds_plan[3];
-    bool          ds_ok[3] = {false, false, false};
     // tensor-core matmul for steps of >= tc_min_cols columns (gemm_tc.cuh)
     TcScratch     tc = {};
     bool          tc_ok = false;
     int           tc_min_cols = 16;
-    // CMOLCU_DS_TRACE=1: per-phase timing of CTA 0, summed over steps, printed at exit
-    unsigned long long *ds_trace = nullptr;
-    std::vector<unsigned long long> ds_trace_host;
-    std::vector<double> ds_work_ns, ds_sync_ns;
-    long long ds_trace_steps = 0;
 };
 
 static void set_msg(char *dst, int n, const char *fmt, ...) {
@@ -145,112 +133,6 @@ struct EngineBuilder {
     }
 };
 
-// Phase table of the persistent decode-step kernel, when the model fits its
-// constraints (fused q/k/v of one dtype, no QK-norm, d_head 64 or 128).
-// Opt-in with CMOLCU_STEP_KERNEL=1: measured on B200 it is still slower than
-// the per-kernel path with programmatic dependent launch (its grid barriers
-// and per-phase activation reads cost more than a kernel boundary), so by
-// default every step runs as separate launches.
-static void step_kernel_note(const char *fmt, ...) {
-    const char *v = getenv("CMOLCU_VERBOSE");
-    if (!v || v[0] != '1') return;
-    va_list ap;
-    va_start(ap, fmt);
-    fprintf(stderr, "[cmolcu] step kernel: ");
-    vfprintf(stderr, fmt, ap);
-    fprintf(stderr, "\n");
-    va_end(ap);
-}
-
-static void build_step_kernel(Engine *e, Engine::Impl *d, EngineBuilder &b) {
-    const char *env = getenv("CMOLCU_STEP_KERNEL");
-    if (!env || env[0] != '1') { step_kernel_note("off (set CMOLCU_STEP_KERNEL=1 to use it)"); return; }
-    const HParams &hp = d->hp;
-    const EngineOptions &o = e->options();
-    const int D = hp.d_model, F = hp.d_ffn, V = hp.vocab_size;
-    const int hd = hp.d_head, nkv = hp.n_kv_heads, KVD = nkv * hd;
-    if (hd != 64 && hd != 128) { step_kernel_note("off (d_head %d)", hd); return; }
-    for (const Layer &ly : d->layers)
-        if (!ly.fused_qkv || ly.q_norm || ly.k_norm) { step_kernel_note("off (separate q/k/v or QK-norm)"); return; }
-    std::vector<DsPhase> ph;
-    GemvArgs g = {};
-    g.x_inc = 1;
-    g.y_inc = 1;
-    g.eps = hp.rms_norm_eps;
-    for (int l = 0; l < hp.n_layers; l++) {
-        const Layer &ly = d->layers[(size_t)l];
-        const bool nope = hp.no_rope_layer_interval > 0 && (l + 1) % hp.no_rope_layer_interval == 0;
-        DsPhase p = {};
-        p.kind = DS_GEMV;
-        p.epi = EPI_QKV;
-        p.g = g;
-        p.g.w = ly.qkv.q;
-        p.g.x = d->x; p.g.x_ld = D;
-        p.g.norm_w = ly.attn_norm;
-        p.g.y = d->qbuf; p.g.y_ld = D;
-        EpiQKV &q = p.g.qkv;
-        q.d_model = D; q.kv_dim = KVD; q.d_head = hd; q.n_kv = nkv; q.page_tokens = o.page_tokens;
-        q.layer = l; q.rope = nope ? 0 : 1; q.rope_cs = d->rope_cs; q.row_base = 0;
-        q.pos = d->meta.pos; q.slot = d->meta.slot; q.page_table = d->page_table; q.max_pages = e->max_pages();
-        q.kv_pages = d->kv_pages; q.page_floats = d->page_floats; q.n_pages = (int)d->n_pages;
-        ph.push_back(p);
-        DsPhase at = {};
-        at.kind = DS_ATTN;
-        at.layer = l;
-        ph.push_back(at);
-        p = DsPhase{};
-        p.kind = DS_GEMV; p.epi = EPI_RESID; p.g = g;
-        p.g.w = ly.wo.q; p.g.x = d->attn; p.g.x_ld = D; p.g.y = d->x; p.g.y_ld = D;
-        ph.push_back(p);
-        p = DsPhase{};
-        p.kind = DS_GEMV; p.epi = EPI_SWIGLU; p.g = g;
-        p.g.w = ly.gu.q; p.g.x = d->x; p.g.x_ld = D; p.g.norm_w = ly.ffn_norm; p.g.y = d->h; p.g.y_ld = F;
-        ph.push_back(p);
-        p = DsPhase{};
-        p.kind = DS_GEMV; p.epi = EPI_RESID; p.g = g;
-        p.g.w = ly.down.q; p.g.x = d->h; p.g.x_ld = F; p.g.y = d->x; p.g.y_ld = D;
-        ph.push_back(p);
-    }
-    {
-        DsPhase p = {};
-        p.kind = DS_GEMV; p.epi = EPI_STORE; p.g = g;
-        p.g.w = d->head.base ? d->head.q : d->embd.q;
-        p.g.x = d->x; p.g.x_ld = D; p.g.norm_w = d->out_norm; p.g.y = d->logits; p.g.y_ld = V;
-        ph.push_back(p);
-    }
-    ds_partition(ph.data(), (int)ph.size(), device_sm_count());
-    const int G = hp.n_heads / nkv;
-    const int ncs[3] = {1, 2, 4};
-    bool any = false;
-    for (int i = 0; i < 3; i++) {
-        d->ds_ok[i] = ncs[i] <= o.max_batch &&
-                      ds_plan(ph.data(), (int)ph.size(), ncs[i], hd, G, o.split_tokens, e->max_pages(), d->ds_plan[i]);
-        any = any || d->ds_ok[i];
-        step_kernel_note("nc %d: %s (slots %d x %d B, union %d B, smem %zu B, grid %d)", ncs[i],
-                         d->ds_ok[i] ? "on" : "off", d->ds_plan[i].nslot, d->ds_plan[i].slot_bytes,
-                         d->ds_plan[i].union_bytes, d->ds_plan[i].smem, d->ds_plan[i].grid);
-    }
-    if (!any) return;
-    d->ds_phases = b.dalloc<DsPhase>(ph.size());
-    d->ds_sync = b.dalloc<unsigned int>(1);
-    if (!d->ds_phases || !d->ds_sync ||
-        cudaMemcpyAsync(d->ds_phases, ph.data(), ph.size() * sizeof(DsPhase), cudaMemcpyHostToDevice, d->stream) !=
-            cudaSuccess ||
-        cudaStreamSynchronize(d->stream) != cudaSuccess) {
-        for (int i = 0; i < 3; i++) d->ds_ok[i] = false;
-        cudaGetLastError();
-        return;
-    }
-    d->ds_nphases = (int)ph.size();
-    const char *tr = getenv("CMOLCU_DS_TRACE");
-    if (tr && tr[0] == '1') {
-        d->ds_trace = b.dalloc<unsigned long long>(6 * ph.size() + 1);
-        d->ds_trace_host.assign(6 * ph.size() + 1, 0);
-        d->ds_work_ns.assign(6 * 5, 0.0);
-        d->ds_sync_ns.assign(6, 0.0);
-    }
-}
-
 // Scratch of the tensor-core matmul, sized for the largest weight at
 // max_batch columns.  Steps of at least tc_min_cols columns use it for every
 // weight in a format it handles (Q4_K, Q8_0, Q4_0, Q5_0); the rest, and
@@ -310,7 +192,8 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     // split (in whole pages) until it fits
     auto q_chunk = [&](int split) { return o.max_group > 1 ? attention_q_chunk(hd, hp.n_heads / nkv, split) : 1; };
     while (e->opt_.split_tokens > o.page_tokens &&
-           attention_smem_bytes(hd, hp.n_heads / nkv, e->opt_.split_tokens, q_chunk(e->opt_.split_tokens)) >
+           attention_smem_bytes(hd, hp.n_heads / nkv, e->opt_.split_tokens, q_chunk(e->opt_.split_tokens),
+                                o.kv_f16 ? 2 : 4) >
                CMOLCU_ATTN_SMEM_MAX)
         e->opt_.split_tokens -= o.page_tokens;
     e->vocab_ = V;
@@ -452,24 +335,24 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     // ---- KV page pool ------------------------------------------------------
     const int P = o.page_tokens;
     e->max_pages_ = (o.max_ctx + P - 1) / P;
-    d->page_floats = (long long)L * 2 * nkv * P * hd;
-    e->kv_bytes_per_token_ = (long long)L * 2 * KVD * 4;
+    const int kvb = o.kv_f16 ? 2 : 4;
+    d->page_elems = (long long)L * 2 * nkv * P * hd;
+    e->kv_bytes_per_token_ = (long long)L * 2 * KVD * kvb;
     d->page_table = b.dalloc<int>((size_t)o.max_slots * e->max_pages_);
     if (!d->page_table) return fail(-1);
     {
         size_t fr = 0, tot = 0;
         cudaMemGetInfo(&fr, &tot);
-        const size_t page_bytes = (size_t)d->page_floats * 4;
+        const size_t page_bytes = (size_t)d->page_elems * kvb;
         long long want = (long long)o.max_slots * e->max_pages_;
         long long fit = (long long)((double)fr * o.kv_pool_frac / (double)page_bytes);
         long long n = want < fit ? want : fit;
         if (n < e->max_pages_) { set_msg(msg, msg_len, "KV pool: not enough device memory"); return fail(-1); }
-        d->kv_pages = b.dalloc<float>((size_t)n * d->page_floats, false);
+        d->kv_pages = b.dalloc<uint8_t>((size_t)n * page_bytes, false);
         if (!d->kv_pages) { set_msg(msg, msg_len, "KV pool allocation failed"); return fail(-1); }
         e->n_pages_ = (int)n;
         d->n_pages = n;
     }
-    build_step_kernel(e, d, b);
     build_tensor_core_path(e, d, b);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(-1);
     *err = 0;
@@ -478,16 +361,6 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
 
 Engine::~Engine() {
     if (!d) return;
-    if (d->ds_trace && d->ds_trace_steps > 0) {
-        static const char *names[6] = {"qkv", "attn", "wo", "gu", "down", "head"};
-        const double n = (double)d->ds_trace_steps;
-        fprintf(stderr, "[cmolcu] step kernel trace over %lld steps (CTA 0, us per step):\n", d->ds_trace_steps);
-        for (int k = 0; k < 6; k++)
-            fprintf(stderr, "  %-5s work %8.2f  sync %8.2f   [stage %7.2f wait %7.2f compute %7.2f epi %7.2f]\n",
-                    names[k], d->ds_work_ns[k] / n / 1e3, d->ds_sync_ns[k] / n / 1e3,
-                    d->ds_work_ns[6 + 4 * k] / n / 1e3, d->ds_work_ns[6 + 4 * k + 1] / n / 1e3,
-                    d->ds_work_ns[6 + 4 * k + 2] / n / 1e3, d->ds_work_ns[6 + 4 * k + 3] / n / 1e3);
-    }
     cudaSetDevice(device_);
     if (d->stream) cudaStreamSynchronize(d->stream);
     for (auto &kv : d->graphs) cudaGraphExecDestroy(kv.second);
@@ -587,44 +460,6 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
     sb.x = d->x;
     sb.d_model = D;
     sb.fault = d->fault;
-    const int dsi = ncol <= 1 ? 0 : ncol <= 2 ? 1 : ncol <= 4 ? 2 : -1;
-    if (only == REC_FULL && dsi >= 0 && d->ds_ok[dsi]) {
-        // one persistent kernel for all layers and the head, between the
-        // step-begin kernel (which also zeroes its barrier counter) and the sampler
-        sb.sync_reset = d->ds_sync;
-        if ((e = step_begin_launch(sb, ncol, st, false)) != cudaSuccess) return e;
-        DsArgs da = {};
-        da.phases = d->ds_phases;
-        da.n_phases = d->ds_nphases;
-        da.ncol = ncol;
-        AttnArgs &at = da.attn;
-        at.q = d->qbuf; at.q_ld = D;
-        at.out = d->attn; at.out_ld = D;
-        at.pos = d->meta.pos; at.slot = d->meta.slot;
-        at.page_table = d->page_table; at.max_pages = max_pages;
-        at.kv_pages = d->kv_pages; at.page_floats = d->page_floats; at.n_pages = (int)d->n_pages;
-        at.fault = d->fault;
-        at.layer = 0; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;
-        at.split_tokens = o.split_tokens; at.n_splits = d->n_splits; at.q_chunk = d->attn_qc; at.grouped = grouped;
-        at.q_block = d->attn_qb;
-        at.scale = 1.0f / sqrtf((float)hd);
-        at.part = d->part; at.counters = d->counters;
-        da.sync_count = d->ds_sync;
-        da.fault = d->fault;
-        da.trace = d->ds_trace;
-        da.rope_cs = d->rope_cs;
-        if ((e = ds_launch(da, d->ds_plan[dsi], hd, st, pdl)) != cudaSuccess) return e;
-        SampleArgs sa = {};
-        sa.meta = d->meta;
-        sa.logits = d->logits;
-        sa.vocab = V;
-        sa.slots = d->slots;
-        sa.out_ids = d->out_dev;
-        sa.fault = d->fault;
-        if ((e = sample_launch(sa, ncol, st, pdl)) != cudaSuccess) return e;
-        launches = 3;
-        return cudaSuccess;
-    }
     if (only == REC_FULL) {
         if ((e = step_begin_launch(sb, ncol, st, false)) != cudaSuccess) return e;
         launches++;
@@ -644,7 +479,8 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         q.d_model = D; q.kv_dim = KVD; q.d_head = hd; q.n_kv = nkv; q.page_tokens = o.page_tokens;
         q.layer = l; q.rope = nope ? 0 : 1; q.rope_cs = d->rope_cs;
         q.pos = d->meta.pos; q.slot = d->meta.slot; q.page_table = d->page_table; q.max_pages = max_pages;
-        q.kv_pages = d->kv_pages; q.page_floats = d->page_floats; q.n_pages = (int)d->n_pages;
+        q.kv_pages = d->kv_pages; q.page_elems = d->page_elems; q.n_pages = (int)d->n_pages;
+        q.kv_f16 = o.kv_f16 ? 1 : 0;
         auto qkv_part = [&](const DevWeight &w, int row_base) -> cudaError_t {
             GemvArgs a = g;
             a.w = w.q;
@@ -682,7 +518,8 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         at.out = d->attn; at.out_ld = D;
         at.pos = d->meta.pos; at.slot = d->meta.slot;
         at.page_table = d->page_table; at.max_pages = max_pages;
-        at.kv_pages = d->kv_pages; at.page_floats = d->page_floats; at.n_pages = (int)d->n_pages;
+        at.kv_pages = d->kv_pages; at.page_elems = d->page_elems; at.n_pages = (int)d->n_pages;
+        at.kv_f16 = o.kv_f16 ? 1 : 0;
         at.fault = d->fault;
         at.layer = l; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;
         at.split_tokens = o.split_tokens; at.n_splits = d->n_splits; at.q_chunk = d->attn_qc; at.grouped = grouped;
@@ -791,10 +628,12 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         m[4 * B + 2 + 3 * u] = 0;
         m[4 * B + 3 + 3 * u] = n_pages_ + 5;
     }
-    last_meta_.assign(m, m + d->meta_ints);
-    last_n_ = n;
-    last_bucket_ = bucket;
-    last_grouped_ = grouped;
+    if (n >= last_n_) {   // the kernel sweeps replay the widest step since the last stats reset
+        last_meta_.assign(m, m + d->meta_ints);
+        last_n_ = n;
+        last_bucket_ = bucket;
+        last_grouped_ = grouped;
+    }
     cudaError_t e = cudaMemcpyAsync(d->meta_dev, d->meta_host, d->meta_ints * sizeof(int), cudaMemcpyHostToDevice,
                                     d->stream);
     if (e == cudaSuccess) e = cudaEventRecord(d->ev0, d->stream);
@@ -844,25 +683,6 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         cudaStreamSynchronize(d->stream);
         snprintf(err_, sizeof err_, "step: device fault code %u", fault);
         return -1;
-    }
-    if (d->ds_trace && d->launches == 3 &&
-        cudaMemcpy(d->ds_trace_host.data(), d->ds_trace, d->ds_trace_host.size() * 8, cudaMemcpyDeviceToHost) ==
-            cudaSuccess) {
-        // phase kinds in table order: QKV ATTN WO GU DOWN per layer, then HEAD
-        const auto &t = d->ds_trace_host;
-        for (int p = 0; p < d->ds_nphases; p++) {
-            const int kind = p == d->ds_nphases - 1 ? 5 : p % 5;
-            d->ds_work_ns[kind] += (double)(t[2 * p + 1] - t[2 * p]);
-            if (p + 1 < d->ds_nphases) d->ds_sync_ns[kind] += (double)(t[2 * p + 2] - t[2 * p + 1]);
-            const unsigned long long *sb = &t[2 * d->ds_nphases + 1 + 4 * p];
-            if (kind != 1 && sb[0] && sb[3]) {   // GEMV sub-steps: staging, first wait, compute, epilogue
-                d->ds_work_ns[6 + 4 * kind + 0] += (double)(sb[0] - t[2 * p]);
-                d->ds_work_ns[6 + 4 * kind + 1] += (double)(sb[1] - sb[0]);
-                d->ds_work_ns[6 + 4 * kind + 2] += (double)(sb[2] - sb[1]);
-                d->ds_work_ns[6 + 4 * kind + 3] += (double)(sb[3] - sb[2]);
-            }
-        }
-        d->ds_trace_steps++;
     }
     float ms = 0.f;
     cudaEventElapsedTime(&ms, d->ev0, d->ev1);

@@ -25,6 +25,7 @@ struct EngineOptions {
     bool  use_graphs = true;
     int   split_tokens = 64;   // attention context split (tokens per work item)
     int   max_group = 1;       // most columns of one session in a step (prefill chunk)
+    bool  kv_f16 = false;      // KV pool in f16 (values rounded to nearest on write) instead of f32
 };
 
 struct SamplerParams {
@@ -88,7 +89,8 @@ class Engine {
     // (graph, CUDA events); bytes = GGUF bytes of all matrices streamed.
     int gemv_sweep(int reps, double *ms_per_pass, long long *bytes_per_pass, int *launches_per_pass);
 
-    // One kernel class of the LAST step, replayed alone `reps` times from a
+    // One kernel class of the widest step since the last reset_stats (the
+    // latest of equal width), replayed alone `reps` times from a
     // CUDA graph (device time per pass by CUDA events on the engine stream):
     //   what 0: its weight products at its width (columns marked inactive,
     //           so no KV is written); bytes = GGUF bytes of every matrix,
@@ -107,7 +109,7 @@ class Engine {
     // Device fault code of the last failed step (0 = none since load).
     unsigned int last_fault() const { return last_fault_; }
     EngineStats stats;
-    void reset_stats() { stats = EngineStats(); }
+    void reset_stats() { stats = EngineStats(); last_n_ = 0; }
     unsigned int fault_code();   // device fault word (0 = none); clears it
 
     struct Impl;      // device state (engine.cu)

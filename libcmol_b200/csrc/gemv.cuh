@@ -52,10 +52,23 @@ struct EpiQKV {
     const int   *slot;          // [ncol] session slot -> page-table row
     const int   *page_table;    // [slots][max_pages]
     int          max_pages;
-    float       *kv_pages;      // page pool
-    long long    page_floats;   // floats per page
+    void        *kv_pages;      // page pool (f32, or f16 when kv_f16)
+    long long    page_elems;    // K/V values per page
     int          n_pages;       // pages in the pool (bounds check)
+    int          kv_f16;        // 1: values stored rounded to f16 (nearest, ties to even)
 };
+
+// Stores the pair (v0, v1) at value index `off` of the KV pool.  off is even,
+// so an f16 pair is one aligned 4-byte store.
+__device__ __forceinline__ void kv_store_pair(const EpiQKV &e, long long off, float v0, float v1) {
+    if (e.kv_f16) {
+        *reinterpret_cast<__half2 *>(static_cast<__half *>(e.kv_pages) + off) = __floats2half2_rn(v0, v1);
+    } else {
+        float *p = static_cast<float *>(e.kv_pages) + off;
+        p[0] = v0;
+        p[1] = v1;
+    }
+}
 
 // Stage geometry, computed on the host for one launch.
 struct PipeCfg {
@@ -322,9 +335,9 @@ __device__ __forceinline__ void epi_qkv_apply(const GemvArgs &a, int lrow, int c
         return;
     }
     const int t = pos % e.page_tokens;
-    float *base = e.kv_pages + (long long)pg * e.page_floats +
-                  ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd + dim;
-    base[0] = v0; base[1] = v1;
+    kv_store_pair(e, (long long)pg * e.page_elems +
+                         ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd + dim,
+                  v0, v1);
 }
 
 __device__ __forceinline__ void epi_qkv_pair(const GemvArgs &a, int lrow, int col, float v0, float v1) {

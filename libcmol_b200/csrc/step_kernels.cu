@@ -61,7 +61,6 @@ __global__ void k_step_begin(StepBeginArgs a) {
     pdl_launch_dependents();
     const int col = blockIdx.x;
     if (col == 0) {
-        if (threadIdx.x == 0 && a.sync_reset) *a.sync_reset = 0u;
         const int n = *a.meta.n_upd;
         for (int u = threadIdx.x; u < n; u += blockDim.x) {
             int s = a.meta.upd[3 * u], idx = a.meta.upd[3 * u + 1], pg = a.meta.upd[3 * u + 2];
@@ -133,14 +132,18 @@ __global__ void k_qknorm(QkNormArgs a, int n_heads) {
     const int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
     if (pg < 0 || pg >= e.n_pages) return;
     const int t = pos % e.page_tokens;
-    float *kp = e.kv_pages + (long long)pg * e.page_floats +
-                ((((long long)e.layer * 2) * e.n_kv + kh) * e.page_tokens + t) * hd;
-    float *vp = e.kv_pages + (long long)pg * e.page_floats +
-                ((((long long)e.layer * 2 + 1) * e.n_kv + kh) * e.page_tokens + t) * hd;
+    const long long ko = (long long)pg * e.page_elems + ((((long long)e.layer * 2) * e.n_kv + kh) * e.page_tokens + t) * hd;
+    const long long vo = ko + (long long)e.n_kv * e.page_tokens * hd;     // the V block follows the K blocks
     const float *vsrc = a.qkv + (long long)col * a.qkv_ld + D + KVD + kh * hd;
     for (int i = 0; i < hd / 32; i++) {
-        kp[lane + 32 * i] = out[i];
-        vp[lane + 32 * i] = vsrc[lane + 32 * i];
+        const int j = lane + 32 * i;
+        if (e.kv_f16) {
+            static_cast<__half *>(e.kv_pages)[ko + j] = __float2half_rn(out[i]);
+            static_cast<__half *>(e.kv_pages)[vo + j] = __float2half_rn(vsrc[j]);
+        } else {
+            static_cast<float *>(e.kv_pages)[ko + j] = out[i];
+            static_cast<float *>(e.kv_pages)[vo + j] = vsrc[j];
+        }
     }
 }
 

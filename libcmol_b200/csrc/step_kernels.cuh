@@ -40,7 +40,6 @@ struct StepBeginArgs {
     float       *x;            // [B][d_model]
     int          d_model;
     unsigned int *fault;       // device fault word
-    unsigned int *sync_reset;  // zeroed by the step (grid barrier counter of the step kernel); may be NULL
 };
 
 struct SampleArgs {

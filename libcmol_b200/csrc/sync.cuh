@@ -18,7 +18,6 @@ enum : unsigned int {
     FAULT_BAD_PAGE = 4,        // a page-table update outside the table / pool
     FAULT_SAMPLE = 5,          // the sampler found no valid candidate (non-finite logits)
     FAULT_ATTN_WAIT = 6,       // attention waited too long for its K/V pages
-    FAULT_GRID_SYNC = 7,       // the decode-step kernel waited too long at a grid barrier
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

@@ -50,7 +50,7 @@ class GenParams(C.Structure):
 
 class CudaOptions(C.Structure):
     _fields_ = [("kv_page_tokens", C.c_int), ("kv_pool_frac", C.c_float),
-                ("max_batch", C.c_int), ("use_graphs", C.c_int)]
+                ("max_batch", C.c_int), ("use_graphs", C.c_int), ("kv_dtype", C.c_int)]
 
 
 class CudaStats(C.Structure):
@@ -130,12 +130,13 @@ class Model:
     """cmol_load / cmol_free around one GGUF file."""
 
     def __init__(self, path: str, max_ctx: int = 2048, max_sessions: int = 4, devices=None,
-                 page_tokens: int = 0, max_batch: int = 0, use_graphs: bool = True, log=None):
+                 page_tokens: int = 0, max_batch: int = 0, use_graphs: bool = True, log=None,
+                 kv_dtype: int = 0):
         L = api()
         if devices is not None:
             arr = (C.c_int * len(devices))(*devices)
             _chk(L.cmol_cuda_set_devices(arr, len(devices)), "cmol_cuda_set_devices")
-        opt = CudaOptions(page_tokens, 0.0, max_batch, 1 if use_graphs else 0)
+        opt = CudaOptions(page_tokens, 0.0, max_batch, 1 if use_graphs else 0, kv_dtype)
         L.cmol_cuda_set_options(C.byref(opt))
         self._log_cb = LOG_FN(lambda lvl, msg, ud: log(lvl, msg.decode())) if log else None
         cfg = Config(max_ctx, max_sessions, 512,
