@@ -42,6 +42,14 @@ def oracle_f16():
 
 
 @pytest.fixture(scope="module")
+def cfg_path(tmp_path_factory):
+    """Config-shape model files, written once per module on first use."""
+    d = str(tmp_path_factory.mktemp("f16cfg"))
+    mg = _mg()
+    return lambda c: mg.config_path(c, d)
+
+
+@pytest.fixture(scope="module")
 def paths(tmp_path_factory):
     d = str(tmp_path_factory.mktemp("f16kv"))
     mg = _mg()
@@ -139,13 +147,12 @@ def test_f16_kv_long_context_and_prefill(gpu, tmp_path, oracle_f16, name):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("c", [1, 3, 4])
-def test_f16_kv_config_shapes(gpu, tmp_path, c):
+def test_f16_kv_config_shapes(gpu, cfg_path, c):
     """The configs' layer shapes with the f16 cache, every position against
     the reference's f32-cache logits (spec tolerance), and 16-column steps
     (tensor cores) at staggered positions."""
     from libcmol_b200.model import Model
-    mg = _mg()
-    path = mg.config_path(c, str(tmp_path))
+    path = cfg_path(c)
     gold = np.load(os.path.join(GOLD, "configs.npz"))
     toks = gold[f"c{c}_tokens"]
 
@@ -177,12 +184,11 @@ def test_f16_kv_config_shapes(gpu, tmp_path, c):
 @pytest.mark.gpu
 @pytest.mark.parametrize("c", [1, 3, 4])
 @pytest.mark.parametrize("tag", ["greedy", "topp"])
-def test_f16_kv_config_streams_match_reference(gpu, tmp_path_factory, c, tag):
+def test_f16_kv_config_streams_match_reference(gpu, cfg_path, c, tag):
     """With the f16 cache, the configs' greedy and seeded top-p streams are
     still the reference's own (f32 cache) streams."""
     from libcmol_b200.model import GenParams, Model
-    mg = _mg()
-    path = mg.config_path(c, str(tmp_path_factory.mktemp(f"s{c}{tag}")))
+    path = cfg_path(c)
     gold = np.load(os.path.join(GOLD, "configs.npz"))
     p = {"greedy": GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=12),
          "topp": GenParams.make(0.9, top_p=0.9, top_k=40, seed=77, repeat_penalty=1.1, max_new_tokens=12)}[tag]
