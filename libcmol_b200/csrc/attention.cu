@@ -1,5 +1,6 @@
 // attention.cu — standalone launch of the split-context GQA decode attention
 // item (attention_item.cuh): one CTA per (split, kv head, column).
+#include "attention_decode.cuh"
 #include "attention_item.cuh"
 #include "gemv_launch.cuh"
 
@@ -189,13 +190,70 @@ static cudaError_t launch_e(const AttnArgs &a, int ncol, size_t smem, cudaStream
     return launch_k(k_attn<E, H>, dim3(a.n_splits, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a);
 }
 
-cudaError_t attention_launch(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl) {
+// Ring stages of the decode kernel: about 96 KB of K / V in flight per CTA
+// (two CTAs an SM), at least two stages.
+static int dec_stages(int hd, int kvb) {
+    const size_t stage = (size_t)2 * DEC_SUB * hd * kvb;
+    int s = (int)((96 * 1024) / stage);
+    return s < 2 ? 2 : s > 4 ? 4 : s;
+}
+
+template <int E, bool H, int GP>
+static cudaError_t launch_dec(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl) {
+    const int kvb = H ? 2 : 4, stages = dec_stages(32 * E, kvb);
+    const size_t smem = dec_smem_bytes(32 * E, kvb, GP, stages);
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_dec<E, H, GP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+    }
+    const int n_chunks = (a.n_splits * a.split_tokens + a.chunk_tokens - 1) / a.chunk_tokens;
+    return launch_k(k_attn_dec<E, H, GP>, dim3(n_chunks, a.n_kv, ncol), dim3(ATTN_THREADS), smem, st, pdl, a,
+                    stages);
+}
+
+template <int E, bool H>
+static cudaError_t launch_dec_g(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl) {
+    switch (dec_pow2(a.n_heads / a.n_kv)) {
+    case 1: return launch_dec<E, H, 1>(a, ncol, st, pdl);
+    case 2: return launch_dec<E, H, 2>(a, ncol, st, pdl);
+    case 4: return launch_dec<E, H, 4>(a, ncol, st, pdl);
+    default: return launch_dec<E, H, 8>(a, ncol, st, pdl);
+    }
+}
+
+cudaError_t attention_launch(const AttnArgs &a_in, int ncol, cudaStream_t st, bool pdl) {
+    AttnArgs a = a_in;
     const int G = a.n_heads / a.n_kv;
     if (a.n_heads % a.n_kv != 0 || G > ATTN_MAX_G) return cudaErrorInvalidValue;
     if (a.split_tokens % a.page_tokens != 0 || a.n_splits < 1) return cudaErrorInvalidValue;
     if (a.q_chunk < 1 || a.q_chunk > ATTN_QB || a.q_block < 1 || a.q_block > ATTN_QB) return cudaErrorInvalidValue;
     // the group layout (a superset of the one-query layout) bounds both kernels
     const int kvb = a.kv_f16 ? 2 : 4;
+    static const bool force_list = [] {
+        const char *v = getenv("CMOLCU_ATTN_LIST");
+        return v && v[0] == '1';
+    }();
+    static const bool split_items = [] {
+        const char *v = getenv("CMOLCU_ATTN_DECODE");
+        return v && v[0] == '0';
+    }();
+    // Decode steps (one token per session): the streaming kernel of
+    // attention_decode.cuh, with chunks of 64..512 tokens, longer when the
+    // step has more (column, kv head) pairs to spread over the SMs.
+    if (!a.grouped && !force_list && !split_items && (a.d_head == 64 || a.d_head == 128) &&
+        DEC_SUB % a.page_tokens == 0 && a.split_tokens <= DEC_SUB) {
+        int subs = 1;
+        while (subs < 8 && ncol * a.n_kv >= 64 * subs) subs <<= 1;
+        a.chunk_tokens = DEC_SUB * subs;
+        const bool h = a.kv_f16 != 0;
+        if (a.d_head == 64) return h ? launch_dec_g<2, true>(a, ncol, st, pdl) : launch_dec_g<2, false>(a, ncol, st, pdl);
+        return h ? launch_dec_g<4, true>(a, ncol, st, pdl) : launch_dec_g<4, false>(a, ncol, st, pdl);
+    }
     if (attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk, kvb) > CMOLCU_ATTN_SMEM_MAX)
         return cudaErrorInvalidValue;
     const size_t smem = a.grouped ? attention_smem_bytes(a.d_head, G, a.split_tokens, a.q_chunk, kvb)

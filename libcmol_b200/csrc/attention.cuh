@@ -33,6 +33,7 @@ struct AttnArgs {
     int          q_chunk;        // queries per shared-memory chunk of a prefill group (>= 1)
     int          grouped;        // 1: a session's consecutive columns share K / V loads
     int          q_block;        // queries per leader of a group (1..32)
+    int          chunk_tokens;   // decode kernel: context tokens per CTA (set by attention_launch)
     float        scale;          // 1/sqrt(d_head)
     float       *part;           // scratch [ncol][n_heads][n_splits][d_head + 2]
     int         *counters;       // scratch [ncol][n_kv], zero between launches

@@ -101,11 +101,14 @@ def test_teacher_forced_logits_tensor_cores(gpu, golden, paths, name, monkeypatc
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("env", [{"CMOLCU_ATTN_LIST": "1"}, {"CMOLCU_ATTN_DECODE": "0"}],
+                         ids=["work_list", "split_items"])
 @pytest.mark.parametrize("name", ["q4_k", "smollm3"])
-def test_attention_work_list_launch(gpu, golden, paths, name):
-    """The work-list attention launch (used for wide steps), forced on every
-    step in a fresh process: teacher-forced logits and greedy streams as the
-    grid launch gives them."""
+def test_attention_work_list_launch(gpu, golden, paths, name, env):
+    """The other decode attention launches, forced on every step in a fresh
+    process: the work-list launch, and the per-split items (the path of
+    head sizes and page sizes the streaming decode kernel does not take).
+    Teacher-forced logits and greedy streams as the default gives them."""
     import subprocess
     import sys
     code = f"""
@@ -123,8 +126,8 @@ with Model({paths[name]!r}, max_ctx=64, max_sessions=2, page_tokens=4) as m:
     assert rc == 0 and ids == g["{name}_gen_greedy"].tolist(), ids
 print("ok")
 """
-    env = dict(os.environ, CMOLCU_ATTN_LIST="1")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, **env), capture_output=True, text=True,
+                       timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
 
 
