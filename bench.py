@@ -92,7 +92,18 @@ def batched_plan(args, rank, world):
     # the workload's bounds (the same on every rank), not from this rank's draw
     ctx_model = int(max(1, hi * args.prompt_scale) + wl["gen"][1] + 8)
     spec = synth.baseline_spec(wl["cfg"], ctx=max(ctx, ctx_model, 256))
+    if getattr(args, "layers", 0) > 0:   # reduced depth for profiling captures (never the reported line)
+        spec.n_layers = args.layers
+        spec.name += f"-L{args.layers}"
     return sessions, plen, glen, ctx, spec, rng
+
+
+def profiler(on):
+    """cudaProfilerStart / Stop (ncu --profile-from-start off captures only
+    the launches in between): the timed region of --profile-timed runs."""
+    import ctypes
+    rt = ctypes.CDLL("libcudart.so.12")
+    (rt.cudaProfilerStart if on else rt.cudaProfilerStop)()
 
 
 def run_batched(args, rank, world, local, barrier, dist=None):
@@ -203,9 +214,13 @@ def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
         clocks.start()
         barrier()
         m.reset_stats()
+        if args.profile_timed:
+            profiler(True)
         t0 = time.perf_counter()
         outs = m.generate_batch(ss, [[t] for t in last], [greedy(K)] * sessions)
         t1 = time.perf_counter()
+        if args.profile_timed:
+            profiler(False)
         barrier()
         clocks.stop()
         assert all(len(o) == K for o in outs), [len(o) for o in outs]
@@ -260,7 +275,8 @@ def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
         "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32 (f16 tensor-core products)", "data": "synthetic",
-        "config": {"workload": wl["label"], "model": spec.name, "sessions": int(ses_all),
+        "config": {"workload": wl["label"] + (f" (PROFILING: {args.layers} layers)" if args.layers else ""),
+                   "model": spec.name, "sessions": int(ses_all),
                    "sessions_per_gpu": sessions, "kv_cache": kv_format_name(args.kv),
                    "mean_context_timed": round(ctx_sum / max(1, ses_all) + K / 2, 1),
                    "decode_steps_timed": int(steps_max),
@@ -807,6 +823,9 @@ def main():
                     help="KV cache format of config 4: 0 = f32 (the reference's), 1 = f16 (default; logits "
                          "within the 2e-2 / 0.9999 parity tolerance, tests/test_kv_f16_gpu.py)")
     ap.add_argument("--no-nested", action="store_true", help="skip the nested config-2 single-session line")
+    ap.add_argument("--layers", type=int, default=0, help="c4: reduced model depth (profiling captures only)")
+    ap.add_argument("--profile-timed", action="store_true",
+                    help="c4: cudaProfilerStart/Stop around the timed steps (ncu --profile-from-start off)")
     ap.add_argument("--ref-steps", type=int, default=24)
     ap.add_argument("--ref-prompt", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -684,23 +684,35 @@ static cmol_err_t submit_and_wait(cmol_session_t *s, Request &r, cmol_id_cb_t cb
     return r.status;
 }
 
-static cmol_err_t generate_ids_impl(cmol_session_t *s, const int32_t *prompt, int n_prompt,
-                                    const cmol_gen_params_t *params, cmol_id_cb_t cb_id, cmol_token_cb_t cb_txt,
-                                    void *ud) {
+// The checks and set-up of one generation request (src/api.c:420-436):
+// context-full check, prompt clamped to the free context, token ids in
+// range.  *empty: nothing to run (an empty prompt), the call returns OK.
+static cmol_err_t prepare_request(cmol_session_t *s, const int32_t *prompt, int n_prompt,
+                                  const cmol_gen_params_t *params, Request &r, bool *empty) {
     static const cmol_gen_params_t def = CMOL_DEFAULT_PARAMS;
+    *empty = false;
     if (!s || (!prompt && n_prompt > 0) || n_prompt < 0) return CMOL_ERR_ARGS;
     if (!params) params = &def;
     cmol_model_t *m = s->model;
     if (s->n_tokens >= m->cfg.max_ctx) return CMOL_ERR_CTX_FULL;   // src/api.c:426
-    if (n_prompt == 0) return CMOL_OK;
+    if (n_prompt == 0) { *empty = true; return CMOL_OK; }
     const int avail = m->cfg.max_ctx - s->n_tokens;
     if (n_prompt > avail) n_prompt = avail;
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= m->vocab) return CMOL_ERR_ARGS;
-    Request r;
     r.prompt.assign(prompt, prompt + n_prompt);
     r.params = *params;
     r.max_new = params->max_new_tokens < 0 ? m->cfg.max_ctx : params->max_new_tokens;
+    return CMOL_OK;
+}
+
+static cmol_err_t generate_ids_impl(cmol_session_t *s, const int32_t *prompt, int n_prompt,
+                                    const cmol_gen_params_t *params, cmol_id_cb_t cb_id, cmol_token_cb_t cb_txt,
+                                    void *ud) {
+    Request r;
+    bool empty = false;
+    const cmol_err_t st = prepare_request(s, prompt, n_prompt, params, r, &empty);
+    if (st != CMOL_OK || empty) return st;
     return submit_and_wait(s, r, cb_id, cb_txt, ud);
 }
 
@@ -775,22 +787,52 @@ extern "C" cmol_err_t cmol_forward_logits_batch(cmol_session_t *const *ss, const
 
 extern "C" cmol_err_t cmol_generate_batch(cmol_batch_item_t *items, int n) {
     if (!items || n <= 0) return CMOL_ERR_ARGS;
-    std::vector<std::thread> th;
-    th.reserve((size_t)n);
+    // every request is set up first and handed to its GPU's batcher in one
+    // go, so the first step already holds all of them; tokens are collected
+    // when a request has finished (no callback runs)
+    std::vector<std::unique_ptr<Request>> rs((size_t)n);
     for (int i = 0; i < n; i++) {
-        th.emplace_back([it = &items[i]]() {
-            it->n_out = 0;
-            auto cb = [](int32_t t, int, void *ud) -> int {
-                cmol_batch_item_t *x = (cmol_batch_item_t *)ud;
-                if (x->n_out < x->out_cap) x->out[x->n_out] = t;
-                x->n_out++;
-                return 0;
-            };
-            it->status = cmol_generate_ids(it->session, it->prompt, it->n_prompt, it->params, cb, it);
-            if (it->n_out > it->out_cap) it->n_out = it->out_cap;
-        });
+        cmol_batch_item_t &it = items[i];
+        it.n_out = 0;
+        std::unique_ptr<Request> r(new Request());
+        bool empty = false;
+        it.status = prepare_request(it.session, it.prompt, it.n_prompt, it.params, *r, &empty);
+        if (it.status != CMOL_OK || empty) continue;
+        r->s = it.session;
+        r->start_n = it.session->n_tokens;
+        rs[(size_t)i] = std::move(r);
     }
-    for (auto &t : th) t.join();
+    std::vector<Worker *> touched;
+    for (int i = 0; i < n; i++) {
+        if (!rs[(size_t)i]) continue;
+        cmol_session_t *s = items[i].session;
+        Worker *w = s->model->workers[(size_t)s->gpu].get();
+        if (std::find(touched.begin(), touched.end(), w) == touched.end()) touched.push_back(w);
+    }
+    for (Worker *w : touched) {
+        {
+            std::lock_guard<std::mutex> lk(w->mu);
+            for (int i = 0; i < n; i++) {
+                if (!rs[(size_t)i]) continue;
+                cmol_session_t *s = items[i].session;
+                if (s->model->workers[(size_t)s->gpu].get() == w) w->incoming.push_back(rs[(size_t)i].get());
+            }
+        }
+        w->cv.notify_all();
+    }
+    for (int i = 0; i < n; i++) {
+        Request *r = rs[(size_t)i].get();
+        if (!r) continue;
+        std::unique_lock<std::mutex> lk(r->mu);
+        r->cv.wait(lk, [&] { return r->finished; });
+        cmol_batch_item_t &it = items[i];
+        for (const auto &tk : r->q) {
+            if (it.n_out < it.out_cap) it.out[it.n_out] = tk.first;
+            it.n_out++;
+        }
+        if (it.n_out > it.out_cap) it.n_out = it.out_cap;
+        it.status = r->status;
+    }
     for (int i = 0; i < n; i++)
         if (items[i].status != CMOL_OK) return items[i].status;
     return CMOL_OK;

@@ -216,6 +216,26 @@ static cudaError_t launch_dec(const AttnArgs &a, int ncol, cudaStream_t st, bool
                     stages);
 }
 
+#define PERS_SMEM_BUDGET (227 * 1024)
+
+template <int E>
+static cudaError_t launch_pers(const AttnArgs &a, cudaStream_t st, bool pdl) {
+    const int stages = pers_stages(32 * E, a.max_cols, PERS_SMEM_BUDGET);
+    const size_t smem = pers_fixed_bytes(32 * E, a.max_cols) + (size_t)stages * pers_stage_bytes(32 * E);
+    static int attr_dev = -1;
+    static size_t attr_smem = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev || attr_smem < smem) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_pers<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+        attr_smem = smem;
+    }
+    return launch_k(k_attn_pers<E>, dim3(device_sm_count()), dim3(PERS_THREADS), smem, st, pdl, a, stages,
+                    a.max_cols);
+}
+
 template <int E, bool H>
 static cudaError_t launch_dec_g(const AttnArgs &a, int ncol, cudaStream_t st, bool pdl) {
     switch (dec_pow2(a.n_heads / a.n_kv)) {
@@ -251,6 +271,9 @@ cudaError_t attention_launch(const AttnArgs &a_in, int ncol, cudaStream_t st, bo
         while (subs < 8 && ncol * a.n_kv >= 64 * subs) subs <<= 1;
         a.chunk_tokens = DEC_SUB * subs;
         const bool h = a.kv_f16 != 0;
+        if (h && a.tc_min_cols > 0 && ncol >= a.tc_min_cols && a.order && a.work &&
+            pers_stages(a.d_head, a.max_cols, PERS_SMEM_BUDGET) >= 2)
+            return a.d_head == 64 ? launch_pers<2>(a, st, pdl) : launch_pers<4>(a, st, pdl);
         if (a.d_head == 64) return h ? launch_dec_g<2, true>(a, ncol, st, pdl) : launch_dec_g<2, false>(a, ncol, st, pdl);
         return h ? launch_dec_g<4, true>(a, ncol, st, pdl) : launch_dec_g<4, false>(a, ncol, st, pdl);
     }

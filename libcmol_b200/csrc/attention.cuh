@@ -34,6 +34,15 @@ struct AttnArgs {
     int          grouped;        // 1: a session's consecutive columns share K / V loads
     int          q_block;        // queries per leader of a group (1..32)
     int          chunk_tokens;   // decode kernel: context tokens per CTA (set by attention_launch)
+    // persistent tensor-core variant (f16 pools, steps of >= tc_min_cols columns);
+    // the work plan is step metadata written by the host
+    int          tc_min_cols;    // 0: never
+    const int   *order;          // [B] live columns, longest context first
+    const int   *chunk_pfx;      // [B+1] prefix sums of their chunk counts
+    const int   *attn_n;         // [1] live columns
+    const int   *attn_chunk;     // [1] context tokens per work item (multiple of 64)
+    int         *work;           // [2 * layers] work-queue counters, zero between launches
+    int          max_cols;       // capacity of order / chunk_pfx (the engine's max_batch)
     float        scale;          // 1/sqrt(d_head)
     float       *part;           // scratch [ncol][n_heads][n_splits][d_head + 2]
     int         *counters;       // scratch [ncol][n_kv], zero between launches

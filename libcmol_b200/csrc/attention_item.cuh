@@ -36,17 +36,18 @@ __host__ __device__ inline size_t attn_item_smem_bytes(int d_head, int G, int sp
            (size_t)ATTN_THREADS * 16;
 }
 
-// Four consecutive K or V values (value index 4 * i4) of a shared-memory
-// tile as floats: f32 tiles directly, f16 tiles widened exactly.
-template <bool H>
-__device__ __forceinline__ float4 kv4(const unsigned char *tile, size_t i4) {
+// Values 4c .. 4c+3 of row t (context position pos) of a shared-memory K or
+// V tile of hd-value rows, as floats: f32 tiles directly, f16 tiles (whose
+// 16-byte chunks are swizzled by position, kv_swz) widened exactly.
+template <bool H, int HD>
+__device__ __forceinline__ float4 kv4(const unsigned char *tile, int t, int pos, int c) {
     if constexpr (H) {
-        const uint2 u = reinterpret_cast<const uint2 *>(tile)[i4];
+        const uint2 u = *reinterpret_cast<const uint2 *>(tile + ((size_t)t * HD + kv_swz(pos, 4 * c, HD)) * 2);
         const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
         const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
         return make_float4(lo.x, lo.y, hi.x, hi.y);
     } else {
-        return reinterpret_cast<const float4 *>(tile)[i4];
+        return reinterpret_cast<const float4 *>(tile)[(size_t)t * (HD / 4) + c];
     }
 }
 
@@ -125,7 +126,7 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
 #pragma unroll
             for (int j = 0; j < HD4; j++) {
                 const int c = (j + lane) & (HD4 - 1);
-                const float4 k = kv4<H>(Ks, (size_t)t * HD4 + c), q = qr[c];
+                const float4 k = kv4<H, hd>(Ks, t, t0 + t, c), q = qr[c];
                 d0 = __fmaf_rn(q.x, k.x, d0);
                 d1 = __fmaf_rn(q.y, k.y, d1);
                 d0 = __fmaf_rn(q.z, k.z, d0);
@@ -164,7 +165,7 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
                 const float *p = Sc + g * S;
                 for (int t = 0; t < n; t++) {
                     const float pt_ = p[t];
-                    const float4 v = kv4<H>(Vs, (size_t)t * HD4 + c);
+                    const float4 v = kv4<H, hd>(Vs, t, t0 + t, c);
                     acc.x = __fmaf_rn(pt_, v.x, acc.x);
                     acc.y = __fmaf_rn(pt_, v.y, acc.y);
                     acc.z = __fmaf_rn(pt_, v.z, acc.z);
@@ -184,7 +185,7 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
             const int tb = (int)((long long)n * part / parts), te = (int)((long long)n * (part + 1) / parts);
             for (int t = tb; t < te; t++) {
                 const float pt_ = p[t];
-                const float4 v = kv4<H>(Vs, (size_t)t * HD4 + c);
+                const float4 v = kv4<H, hd>(Vs, t, t0 + t, c);
                 acc.x = __fmaf_rn(pt_, v.x, acc.x);
                 acc.y = __fmaf_rn(pt_, v.y, acc.y);
                 acc.z = __fmaf_rn(pt_, v.z, acc.z);
@@ -377,7 +378,7 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
 #pragma unroll
                     for (int j = 0; j < HD4; j++) {
                         const int cc = (j + lane) & (HD4 - 1);
-                        const float4 k = kv4<H>(Ks, (size_t)t * HD4 + cc), q = qr[cc];
+                        const float4 k = kv4<H, hd>(Ks, t, t0 + t, cc), q = qr[cc];
                         d0 = __fmaf_rn(q.x, k.x, d0);
                         d1 = __fmaf_rn(q.y, k.y, d1);
                         d0 = __fmaf_rn(q.z, k.z, d0);
@@ -423,7 +424,7 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int t = tb; t < te; t++) {
                     const float pt_ = p[t];
-                    const float4 v = kv4<H>(Vs, (size_t)t * HD4 + cc);
+                    const float4 v = kv4<H, hd>(Vs, t, t0 + t, cc);
                     acc.x = __fmaf_rn(pt_, v.x, acc.x);
                     acc.y = __fmaf_rn(pt_, v.y, acc.y);
                     acc.z = __fmaf_rn(pt_, v.z, acc.z);

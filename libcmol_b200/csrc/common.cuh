@@ -46,6 +46,17 @@ __host__ __device__ inline size_t dt_row_bytes(int k, int dt) {
     return bv ? (size_t)(k / bv) * (size_t)dt_block_bytes(dt) : 0;
 }
 
+// f16 KV pages store each token's d_head values with their 16-byte chunks
+// (8 values) permuted by the token's position in the context: chunk c of the
+// token at position pos sits at chunk c ^ (pos & m), m = min(7, chunks per
+// row - 1).  Eight consecutive positions then place any one chunk in eight
+// different bank groups, so the tensor-core fragment loads (ldmatrix) of K
+// and V tiles are free of bank conflicts.  Stored index of value d.
+__host__ __device__ __forceinline__ int kv_swz(int pos, int d, int hd) {
+    const int m = hd >= 64 ? 7 : (hd >> 3) - 1;
+    return (((d >> 3) ^ (pos & m)) << 3) | (d & 7);
+}
+
 // Shared memory is a dynamic extern buffer in every kernel.
 extern __shared__ __align__(16) unsigned char cmolcu_smem[];
 

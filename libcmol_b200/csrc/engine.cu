@@ -5,6 +5,7 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -54,6 +55,7 @@ struct Engine::Impl {
     float *x = nullptr, *qbuf = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *qkvbuf = nullptr;
     float *part = nullptr;
     int   *counters = nullptr;
+    int   *work = nullptr;          // [2 * layers] attention work-queue counters
     unsigned int *fault = nullptr;
     int    n_splits = 1;
     int    attn_qc = 1;        // attention queries per chunk of a prefill group
@@ -313,7 +315,7 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     d->counters = b.dalloc<int>((size_t)B * nkv);
 
     d->slots = b.dalloc<SlotSampler>((size_t)o.max_slots);
-    d->meta_ints = (size_t)4 * B + 1 + 3 * (size_t)B;
+    d->meta_ints = (size_t)4 * B + 1 + 3 * (size_t)B + B + (B + 1) + 2;
     d->meta_dev = b.dalloc<int>(d->meta_ints);
     d->out_dev = b.dalloc<int>((size_t)B + 1);   // + the fault word, read back with the ids
     d->fault = reinterpret_cast<unsigned int *>(d->out_dev + B);
@@ -331,6 +333,12 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     d->meta.sample = d->meta_dev + 3 * B;
     d->meta.n_upd = d->meta_dev + 4 * B;
     d->meta.upd = d->meta_dev + 4 * B + 1;
+    d->meta.order = d->meta_dev + 7 * B + 1;
+    d->meta.chunk_pfx = d->meta_dev + 8 * B + 1;
+    d->meta.attn_n = d->meta_dev + 9 * B + 2;
+    d->meta.attn_chunk = d->meta_dev + 9 * B + 3;
+    d->work = b.dalloc<int>((size_t)2 * L);
+    if (!d->work) return fail(-1);
 
     // ---- KV page pool ------------------------------------------------------
     const int P = o.page_tokens;
@@ -526,6 +534,10 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         at.q_block = d->attn_qb;
         at.scale = 1.0f / sqrtf((float)hd);
         at.part = d->part; at.counters = d->counters;
+        at.tc_min_cols = d->tc_min_cols;
+        at.order = d->meta.order; at.chunk_pfx = d->meta.chunk_pfx;
+        at.attn_n = d->meta.attn_n; at.attn_chunk = d->meta.attn_chunk;
+        at.work = d->work; at.max_cols = o.max_batch;
         if (!gemv_only) {
             if ((e = attention_launch(at, ncol, st, pdl)) != cudaSuccess) return e;
             launches++;
@@ -579,6 +591,31 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
     return cudaSuccess;
 }
 
+// Work plan of the persistent decode attention (attention_decode.cuh) in the
+// step metadata: the live columns by context length, longest first; the
+// chunk size, the largest power-of-two multiple of 64 tokens (up to 16384)
+// that still gives about six (chunk, kv head) items per SM; and the prefix
+// sums of the columns' chunk counts.
+static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, int n_kv) {
+    int *order = m + 7 * B + 1, *pfx = m + 8 * B + 1;
+    int nl = 0;
+    for (int i = 0; i < (int)cols.size(); i++)
+        if (cols[i].pos >= 0) order[nl++] = i;
+    std::stable_sort(order, order + nl, [&](int x, int y) { return cols[x].pos > cols[y].pos; });
+    const long long target = 6LL * device_sm_count();
+    auto items = [&](int c) {
+        long long t = 0;
+        for (int r = 0; r < nl; r++) t += cols[order[r]].pos / c + 1;
+        return t * n_kv;
+    };
+    int ch = 16384;
+    while (ch > 64 && items(ch) < target) ch >>= 1;
+    pfx[0] = 0;
+    for (int r = 0; r < nl; r++) pfx[r + 1] = pfx[r] + cols[order[r]].pos / ch + 1;
+    m[9 * B + 2] = nl;
+    m[9 * B + 3] = ch;
+}
+
 int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpdate> &upd, int32_t *out_ids,
                  float *logits_out) {
     const int n = (int)cols.size();
@@ -618,6 +655,7 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
     }
     // planted errors of the fault-path tests: both are caught by the bounds
     // checks of k_step_begin, which record the code and skip the access
+    attention_plan(m, cols, B, d->hp.n_kv_heads);
     const int inject = inject_.exchange(0);
     if (inject == 1) {
         m[0] = vocab_ + 3;
@@ -680,6 +718,7 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         cudaMemsetAsync(d->fault, 0, sizeof(unsigned int), d->stream);
         // an abandoned step can leave attention split counters behind
         cudaMemsetAsync(d->counters, 0, (size_t)B * d->hp.n_kv_heads * sizeof(int), d->stream);
+        cudaMemsetAsync(d->work, 0, (size_t)2 * d->hp.n_layers * sizeof(int), d->stream);
         cudaStreamSynchronize(d->stream);
         snprintf(err_, sizeof err_, "step: device fault code %u", fault);
         return -1;

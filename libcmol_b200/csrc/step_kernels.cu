@@ -138,8 +138,9 @@ __global__ void k_qknorm(QkNormArgs a, int n_heads) {
     for (int i = 0; i < hd / 32; i++) {
         const int j = lane + 32 * i;
         if (e.kv_f16) {
-            static_cast<__half *>(e.kv_pages)[ko + j] = __float2half_rn(out[i]);
-            static_cast<__half *>(e.kv_pages)[vo + j] = __float2half_rn(vsrc[j]);
+            const int js = kv_swz(pos, j, hd);
+            static_cast<__half *>(e.kv_pages)[ko + js] = __float2half_rn(out[i]);
+            static_cast<__half *>(e.kv_pages)[vo + js] = __float2half_rn(vsrc[j]);
         } else {
             static_cast<float *>(e.kv_pages)[ko + j] = out[i];
             static_cast<float *>(e.kv_pages)[vo + j] = vsrc[j];

@@ -28,6 +28,10 @@ struct StepMetaPtrs {
     int *sample;     // [B] 1: sample a token from this column's logits
     int *n_upd;      // [1] page-table updates this step
     int *upd;        // [3B] (slot, page index, page id) triples
+    int *order;      // [B] live columns, longest context first (attention work order)
+    int *chunk_pfx;  // [B+1] prefix sums of their attention chunk counts
+    int *attn_n;     // [1] live columns
+    int *attn_chunk; // [1] context tokens per attention work item
 };
 
 struct StepBeginArgs {

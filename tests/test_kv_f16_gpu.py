@@ -197,3 +197,77 @@ def test_f16_kv_config_streams_match_reference(gpu, cfg_path, c, tag):
         rc, ids = s.generate_ids(gold[f"c{c}_tokens"][:6], p)
         assert rc == 0 and ids == gold[f"c{c}_gen_{tag}"].tolist()
         s.release()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", MODELS)
+def test_f16_kv_tensor_core_attention(gpu, paths, monkeypatch, name):
+    """Every step on the tensor cores (CMOLCU_TC_MIN_COLS=1): the weight
+    products and, with the f16 cache, the persistent decode attention (f16
+    queries and probabilities, f32 accumulation).  Logits against the
+    reference's f32 cache at the specified tolerance."""
+    from libcmol_b200.model import Model
+    monkeypatch.setenv("CMOLCU_TC_MIN_COLS", "1")
+    g = np.load(os.path.join(GOLD, "models.npz"))
+    with Model(paths[name], max_ctx=64, max_sessions=2, page_tokens=4, kv_dtype=1) as m:
+        s = m.acquire()
+        worst = 0.0
+        for i, t in enumerate(g[f"{name}_tokens"]):
+            got = s.forward_logits(int(t))
+            ref = g[f"{name}_logits"][i]
+            d = float(np.abs(got - ref).max())
+            worst = max(worst, d)
+            assert d <= ATOL and _cos(got, ref) >= COS, (i, d)
+        print(f"{name}: tensor-core attention, f16 cache: worst max-abs {worst:.2e}")
+        s.release()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["q8_0", "smollm3"])
+def test_f16_kv_tensor_core_attention_long(gpu, tmp_path, monkeypatch, oracle_f16, name):
+    """The persistent tensor-core attention over 400 positions (many 64-token
+    sub-tiles, columns split into several chunks merged in order, partial
+    last sub-tiles), and 16 staggered sessions at once: logits against the
+    f16-cache checker within the specified tolerance."""
+    from libcmol_b200 import synth
+    from libcmol_b200.model import Model
+    from oracle.oracle import OracleModel
+    monkeypatch.setenv("CMOLCU_TC_MIN_COLS", "1")
+    kw = {"q8_0": dict(dtype=8),
+          "smollm3": dict(dtype=12, n_layers=3, arch="smollm3", no_rope_interval=2, rope_base=5e6, qk_norm=True,
+                          tied=False, dt_head=8, n_heads=4, n_kv_heads=1)}[name]
+    dt = kw.pop("dtype")
+    path = str(tmp_path / f"tcattn_{name}.gguf")
+    synth.write_gguf(path, synth.tiny_spec(dt, ctx=512, **kw))
+    rng = np.random.default_rng(9)
+    toks = rng.integers(0, 512, size=400)
+    om = OracleModel(path, lanes=16)
+    os_ = om.session(512)
+    refs = {}
+    for i, t in enumerate(toks):
+        r = om.forward(os_, int(t), i)
+        if i % 23 == 0 or i >= 390:
+            refs[i] = r
+    om.free_session(os_)
+    with Model(path, max_ctx=512, max_sessions=16, kv_dtype=1) as m:
+        s = m.acquire()
+        worst = 0.0
+        for i, t in enumerate(toks):
+            got = s.forward_logits(int(t))
+            if i in refs:
+                d = float(np.abs(got - refs[i]).max())
+                worst = max(worst, d)
+                assert d <= ATOL and _cos(got, refs[i]) >= COS, (i, d)
+        s.release()
+        ss = [m.acquire() for _ in range(16)]
+        for t in range(len(toks) + 15):
+            live = [i for i in range(16) if 0 <= t - i < len(toks)]
+            lg = m.forward_logits_batch([ss[i] for i in live], [int(toks[t - i]) for i in live])
+            for row, i in enumerate(live):
+                if t - i in refs:
+                    d = float(np.abs(lg[row] - refs[t - i]).max())
+                    worst = max(worst, d)
+                    assert d <= ATOL and _cos(lg[row], refs[t - i]) >= COS, (t, i, d)
+        print(f"{name}: tensor-core attention to position 400: worst max-abs {worst:.2e}")
+        for x in ss:
+            x.release()
