@@ -432,8 +432,11 @@ __host__ __device__ inline size_t pers_stage_bytes(int hd) {
     return (size_t)2 * DEC_SUB * hd * 2 + (size_t)ATTN_MAX_G * hd * 4;   // K, V (f16) + query rows (f32)
 }
 __host__ __device__ inline size_t pers_pfx_bytes(int max_cols) { return (((size_t)max_cols + 1) * 4 + 15) / 16 * 16; }
+#define PERS_MAX_ITEM_PAGES 1024   // pages of one work item (the host caps the chunk accordingly)
+
 __host__ __device__ inline size_t pers_fixed_bytes(int hd, int max_cols) {
     return (size_t)ATTN_WARPS * ATTN_MAX_G * (hd + 2) * 4        // warp states
+           + (size_t)PERS_MAX_ITEM_PAGES * 4                     // the current item's page list
            + pers_pfx_bytes(max_cols)                            // chunk prefix sums
            + (size_t)PERS_STAGES_MAX * sizeof(PersMeta) + 16     // stage descriptions, flag
            + (size_t)(2 * PERS_STAGES_MAX + 2) * 8;               // full / empty / combine mbarriers
@@ -455,7 +458,8 @@ __global__ void __launch_bounds__(PERS_THREADS, 1) k_attn_pers(AttnArgs a, int s
 
     unsigned char *ring = cmolcu_smem;
     float *red = reinterpret_cast<float *>(ring + (size_t)stages * sb);                 // [8][8][hd + 2]
-    int *pfx = reinterpret_cast<int *>(red + (size_t)ATTN_WARPS * ATTN_MAX_G * (hd + 2));
+    int *pages = reinterpret_cast<int *>(red + (size_t)ATTN_WARPS * ATTN_MAX_G * (hd + 2));   // [1024]
+    int *pfx = pages + PERS_MAX_ITEM_PAGES;
     PersMeta *meta = reinterpret_cast<PersMeta *>(reinterpret_cast<unsigned char *>(pfx) + pers_pfx_bytes(max_cols));
     int *fail = reinterpret_cast<int *>(meta + PERS_STAGES_MAX);
     uint64_t *full = reinterpret_cast<uint64_t *>(fail + 4);
@@ -482,14 +486,19 @@ __global__ void __launch_bounds__(PERS_THREADS, 1) k_attn_pers(AttnArgs a, int s
     int *work = a.work + 2 * a.layer;                   // [0] next item, [1] consumer warps done
 
     if (warp == ATTN_WARPS) {
-        // ---- producer -------------------------------------------------------------
-        if (lane != 0) return;
-        fence_proxy_async_global();                     // K, V and q of this step came through the generic proxy
-        int k = 0;                                      // stages issued so far
+        // ---- producer warp ----------------------------------------------------------
+        // All 32 lanes load an item's description and page list (into
+        // shared memory, one parallel round); lane 0 issues the copies.  The
+        // next item's index is taken while the current one streams.
+        if (lane == 0) fence_proxy_async_global();      // K, V and q of this step came through the generic proxy
+        const int P = a.page_tokens;
+        int k = 0;                                      // stages issued so far (lane 0's count, broadcast)
         bool bad = false;
-        for (;;) {
-            const int i = *vfail ? total : atomicAdd(&work[0], 1);
-            if (i >= total) break;
+        int nxt = 0;
+        if (lane == 0) nxt = *vfail ? total : atomicAdd(&work[0], 1);
+        nxt = __shfl_sync(0xffffffffu, nxt, 0);
+        while (nxt < total) {
+            const int i = nxt;
             const int u = i / nkv, hk = i % nkv;
             int lo = 0, hi = nlive - 1;                 // column rank: the last r with pfx[r] <= u
             while (lo < hi) {
@@ -498,47 +507,60 @@ __global__ void __launch_bounds__(PERS_THREADS, 1) k_attn_pers(AttnArgs a, int s
             }
             const int col = a.order[lo], chunk = u - pfx[lo];
             const int pos = a.pos[col];
-            const int c0 = chunk * CH, ntok = min(CH, pos + 1 - c0), nsub = (ntok + DEC_SUB - 1) / DEC_SUB;
             const int srow = a.slot ? a.slot[col] : col;
-            const int *pt = a.page_table + (long long)srow * a.max_pages;
-            const int P = a.page_tokens;
-            for (int j = 0; j < nsub; j++, k++) {
-                const int st = k % stages;
-                if (k >= stages &&
-                    !mbar_wait(&empty[st], (uint32_t)(((k / stages) - 1) & 1), a.fault, FAULT_ATTN_WAIT)) {
-                    bad = true;
-                    break;
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                const int t0 = c0 + j * DEC_SUB, n = min(DEC_SUB, c0 + ntok - t0), npg = (n + P - 1) / P;
-                for (int p = 0; p < npg; p++) {
-                    const int pg = pt[t0 / P + p];
-                    if (pg < 0 || pg >= a.n_pages) {
-                        if (a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
-                        bad = true;
-                    }
-                }
-                if (bad) break;
-                unsigned char *stage = ring + (size_t)st * sb;
-                PersMeta &md = meta[st];
-                md.col = col; md.hk = hk; md.chunk = chunk; md.n = n; md.c0 = c0; md.pos = pos;
-                md.flags = (j == 0 ? PM_FIRST : 0) | (j == nsub - 1 ? PM_LAST : 0);
+            const int c0 = chunk * CH, ntok = min(CH, pos + 1 - c0), nsub = (ntok + DEC_SUB - 1) / DEC_SUB;
+            const int npg_item = (ntok + P - 1) / P;    // c0 is a multiple of P (CH is)
+            const int *pt = a.page_table + (long long)srow * a.max_pages + c0 / P;
+            bool lbad = npg_item > PERS_MAX_ITEM_PAGES;
+            for (int p = lane; p < npg_item && !lbad; p += 32) {
+                const int pg = pt[p];
+                if (pg < 0 || pg >= a.n_pages) lbad = true;
+                pages[p] = pg;
+            }
+            if (__any_sync(0xffffffffu, lbad)) {
+                if (lane == 0 && a.fault) atomicExch(a.fault, FAULT_BAD_PAGE);
+                bad = true;
+                break;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                nxt = *vfail ? total : atomicAdd(&work[0], 1);   // in flight while this item streams
                 const uint32_t blk = (uint32_t)(P * hd * 2);
-                const uint32_t qbytes = j == 0 ? (uint32_t)(G * hd * 4) : 0u;
-                mbar_arrive_expect_tx(&full[st], 2u * npg * blk + qbytes);
                 const long long head_off = ((long long)a.layer * 2 * nkv + hk) * P * hd;
                 const long long v_off = (long long)nkv * P * hd;
                 const unsigned char *pool = static_cast<const unsigned char *>(a.kv_pages);
-                for (int p = 0; p < npg; p++) {
-                    const unsigned char *kp = pool + ((long long)pt[t0 / P + p] * a.page_elems + head_off) * 2;
-                    bulk_g2s(stage + (size_t)p * blk, kp, blk, &full[st]);
-                    bulk_g2s(stage + (size_t)DEC_SUB * hd * 2 + (size_t)p * blk, kp + v_off * 2, blk, &full[st]);
+                for (int j = 0; j < nsub; j++, k++) {
+                    const int st = k % stages;
+                    if (k >= stages &&
+                        !mbar_wait(&empty[st], (uint32_t)(((k / stages) - 1) & 1), a.fault, FAULT_ATTN_WAIT)) {
+                        bad = true;
+                        break;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    const int n = min(DEC_SUB, ntok - j * DEC_SUB), npg = (n + P - 1) / P;
+                    const int pg0 = j * (DEC_SUB / P);
+                    unsigned char *stage = ring + (size_t)st * sb;
+                    PersMeta &md = meta[st];
+                    md.col = col; md.hk = hk; md.chunk = chunk; md.n = n; md.c0 = c0; md.pos = pos;
+                    md.flags = (j == 0 ? PM_FIRST : 0) | (j == nsub - 1 ? PM_LAST : 0);
+                    const uint32_t qbytes = j == 0 ? (uint32_t)(G * hd * 4) : 0u;
+                    mbar_arrive_expect_tx(&full[st], 2u * npg * blk + qbytes);
+                    for (int p = 0; p < npg; p++) {
+                        const unsigned char *kp = pool + ((long long)pages[pg0 + p] * a.page_elems + head_off) * 2;
+                        bulk_g2s(stage + (size_t)p * blk, kp, blk, &full[st]);
+                        bulk_g2s(stage + (size_t)DEC_SUB * hd * 2 + (size_t)p * blk, kp + v_off * 2, blk, &full[st]);
+                    }
+                    if (qbytes)
+                        bulk_g2s(stage + kvb, a.q + (long long)col * a.q_ld + (long long)hk * G * hd, qbytes,
+                                 &full[st]);
                 }
-                if (qbytes)
-                    bulk_g2s(stage + kvb, a.q + (long long)col * a.q_ld + (long long)hk * G * hd, qbytes, &full[st]);
             }
+            nxt = __shfl_sync(0xffffffffu, nxt, 0);
+            bad = __shfl_sync(0xffffffffu, bad ? 1 : 0, 0) != 0;
+            __syncwarp();                               // the page list is reused by the next item
             if (bad) break;
         }
+        if (lane != 0) return;
         // the end marker (after a failure too): one more stage, no data
         const int st = k % stages;
         bool can = true;

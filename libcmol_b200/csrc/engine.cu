@@ -593,10 +593,10 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
 
 // Work plan of the persistent decode attention (attention_decode.cuh) in the
 // step metadata: the live columns by context length, longest first; the
-// chunk size, the largest power-of-two multiple of 64 tokens (up to 16384)
+// chunk size, the largest power-of-two multiple of 64 tokens (up to 4096)
 // that still gives about six (chunk, kv head) items per SM; and the prefix
 // sums of the columns' chunk counts.
-static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, int n_kv) {
+static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, int n_kv, int page_tokens) {
     int *order = m + 7 * B + 1, *pfx = m + 8 * B + 1;
     int nl = 0;
     for (int i = 0; i < (int)cols.size(); i++)
@@ -608,7 +608,8 @@ static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, i
         for (int r = 0; r < nl; r++) t += cols[order[r]].pos / c + 1;
         return t * n_kv;
     };
-    int ch = 16384;
+    int ch = 4096;                                // at most 1024 pages an item (its page list in shared memory)
+    while (ch > 1024 * page_tokens) ch >>= 1;
     while (ch > 64 && items(ch) < target) ch >>= 1;
     pfx[0] = 0;
     for (int r = 0; r < nl; r++) pfx[r + 1] = pfx[r] + cols[order[r]].pos / ch + 1;
@@ -655,7 +656,7 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
     }
     // planted errors of the fault-path tests: both are caught by the bounds
     // checks of k_step_begin, which record the code and skip the access
-    attention_plan(m, cols, B, d->hp.n_kv_heads);
+    attention_plan(m, cols, B, d->hp.n_kv_heads, opt_.page_tokens);
     const int inject = inject_.exchange(0);
     if (inject == 1) {
         m[0] = vocab_ + 3;
