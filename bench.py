@@ -396,7 +396,8 @@ def sessions_per_rank(total, world, rank):
 
 
 def model_path(spec):
-    cache = os.environ.get("CMOL_BENCH_CACHE", "/tmp/cmol_bench")
+    import tempfile
+    cache = os.environ.get("CMOL_BENCH_CACHE", os.path.join(tempfile.gettempdir(), "cmol_bench"))
     os.makedirs(cache, exist_ok=True)
     return os.path.join(cache, f"{spec.name}-s{spec.seed}-ctx{spec.ctx}.gguf")
 

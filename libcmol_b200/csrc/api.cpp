@@ -54,6 +54,7 @@ struct Request {
     float               *logits_out = nullptr;
     // progress (worker thread only)
     int  start_n = 0;         // session n_tokens at admission
+    long long budget = 0;     // tokens it may run (prompt + generation cap): its share of the GPU's load
     int  fed = 0;             // prompt tokens already run
     int  last = -1;           // sampled token waiting to be forwarded
     int  n_gen = 0;
@@ -75,8 +76,9 @@ struct Worker;
 
 struct cmol_session {
     cmol_model_t *model = nullptr;
-    int           slot = 0;
+    int           slot = 0;           // index in the model's session table
     int           gpu = 0;
+    int           lslot = 0;          // slot on its GPU's engine (page-table row, sampler state)
     int           n_tokens = 0;       // tokens in the KV cache
     std::vector<int> pages;            // page ids, one per page_tokens positions
 };
@@ -95,6 +97,10 @@ struct Worker {
     std::vector<int>       free_pages;
     bool                   stop = false;
     int                    n_sessions = 0;     // sessions assigned (for placement)
+    std::vector<int>       free_lslots;        // engine slots not held by a session
+    // Placement load: tokens in the KV caches of this GPU's sessions plus
+    // tokens still to run for their requests (prompt and generation budget).
+    std::atomic<long long> load{0};
     void run();
 };
 
@@ -252,7 +258,7 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
         loaders.emplace_back([&, g]() {
             EngineOptions eo;
             const int per_gpu = (ns + ng - 1) / ng;
-            eo.max_slots = ns;
+            eo.max_slots = per_gpu;          // this GPU's share of the sessions
             // columns of a step: one per session, plus up to prefill_chunk
             // (at most 256) further prompt tokens of sessions still in prefill
             const int prefill = std::max(1, std::min(m->cfg.prefill_chunk, 256));
@@ -276,6 +282,8 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
                 std::vector<int> &fp = m->workers[g]->free_pages;
                 fp.resize((size_t)en->n_pages());
                 for (int i = 0; i < en->n_pages(); i++) fp[i] = en->n_pages() - 1 - i;
+                std::vector<int> &fl = m->workers[g]->free_lslots;
+                for (int i = per_gpu - 1; i >= 0; i--) fl.push_back(i);
             }
         });
     }
@@ -317,19 +325,33 @@ extern "C" void cmol_free(cmol_model_t *m) {
 // ---------------------------------------------------------------------------
 // sessions (src/api.c:309-334): lowest free slot, NULL when exhausted
 // ---------------------------------------------------------------------------
+// Placement (scope of the survey's multi-GPU row): a new session goes to
+// the GPU with the least outstanding work — tokens held in its sessions' KV
+// caches plus tokens its queued and running requests still have to run —
+// among those with a free engine slot; ties go to the GPU with fewer
+// sessions, then the lower index.
 extern "C" cmol_session_t *cmol_session_acquire(cmol_model_t *m) {
     if (!m) return nullptr;
     std::lock_guard<std::mutex> lk(m->pool_mu);
     for (size_t i = 0; i < m->slot_free.size(); i++) {
         if (!m->slot_free[i]) continue;
+        int best = -1;
+        for (size_t g = 0; g < m->workers.size(); g++) {
+            Worker *w = m->workers[g].get();
+            if (w->free_lslots.empty()) continue;
+            if (best < 0) { best = (int)g; continue; }
+            Worker *b = m->workers[(size_t)best].get();
+            const long long lw = w->load.load(), lb = b->load.load();
+            if (lw < lb || (lw == lb && w->n_sessions < b->n_sessions)) best = (int)g;
+        }
+        if (best < 0) return nullptr;   // every engine slot is held
         m->slot_free[i] = 0;
         cmol_session_t *s = &m->slots[i];
-        // place on the GPU with the fewest sessions
-        int best = 0;
-        for (size_t g = 1; g < m->workers.size(); g++)
-            if (m->workers[g]->n_sessions < m->workers[best]->n_sessions) best = (int)g;
+        Worker *w = m->workers[(size_t)best].get();
         s->gpu = best;
-        m->workers[best]->n_sessions++;
+        s->lslot = w->free_lslots.back();
+        w->free_lslots.pop_back();
+        w->n_sessions++;
         s->n_tokens = 0;
         return s;
     }
@@ -345,14 +367,17 @@ extern "C" void cmol_session_release(cmol_session_t *s) {
         for (int p : s->pages) w->free_pages.push_back(p);
     }
     s->pages.clear();
+    w->load -= s->n_tokens;
     s->n_tokens = 0;
     std::lock_guard<std::mutex> lk(m->pool_mu);
     w->n_sessions--;
+    w->free_lslots.push_back(s->lslot);
     m->slot_free[(size_t)s->slot] = 1;
 }
 
 extern "C" void cmol_session_reset(cmol_session_t *s) {
     if (!s) return;
+    s->model->workers[(size_t)s->gpu]->load -= s->n_tokens;
     s->n_tokens = 0;   // pages stay with the session for its next turn
 }
 
@@ -446,6 +471,7 @@ void Worker::run() {
     // from `active`, and only then finished, as the worker's last touch.
     std::vector<std::pair<Request *, cmol_err_t>> retired;
     auto retire = [&](Request *r, cmol_err_t st) {
+        load -= r->budget - (r->s->n_tokens - r->start_n);   // what it did not run leaves the load
         r->s = nullptr;
         retired.emplace_back(r, st);
     };
@@ -484,7 +510,7 @@ void Worker::run() {
             for (int i = 0; i < seed_n; i++) sp.ring[i] = r->prompt[(size_t)(np - seed_n + i)];
             sp.ring_head = seed_n % kRepeatBuf;
             sp.ring_fill = seed_n;
-            if (e->set_sampler(r->s->slot, sp)) retire(r, CMOL_ERR_INVALID);
+            if (e->set_sampler(r->s->lslot, sp)) retire(r, CMOL_ERR_INVALID);
         }
         // drop aborted / failed requests
         std::vector<Request *> keep;
@@ -492,6 +518,7 @@ void Worker::run() {
             if (!r->s) continue;
             if (r->abort.load()) {
                 r->s->n_tokens = r->final_n_tokens >= 0 ? r->final_n_tokens : r->s->n_tokens;
+                load -= r->budget - (r->s->n_tokens - r->start_n);
                 finish(r, CMOL_OK);
                 continue;
             }
@@ -523,7 +550,7 @@ void Worker::run() {
             cmol_session_t *s = r->s;
             StepColumn c;
             c.pos = s->n_tokens + off;
-            c.slot = s->slot;
+            c.slot = s->lslot;
             const int np = (int)r->prompt.size();
             if (r->fed + off < np) {
                 c.token = r->prompt[(size_t)(r->fed + off)];
@@ -539,7 +566,7 @@ void Worker::run() {
                 int pg = free_pages.back();
                 free_pages.pop_back();
                 s->pages.push_back(pg);
-                upd.push_back(PageUpdate{s->slot, pidx, pg});
+                upd.push_back(PageUpdate{s->lslot, pidx, pg});
             }
             cols.push_back(c);
             return true;
@@ -644,6 +671,7 @@ static cmol_err_t submit_and_wait(cmol_session_t *s, Request &r, cmol_id_cb_t cb
     Worker *w = m->workers[(size_t)s->gpu].get();
     r.s = s;
     r.start_n = s->n_tokens;
+    w->load += r.budget;
     {
         std::lock_guard<std::mutex> lk(w->mu);
         w->incoming.push_back(&r);
@@ -703,6 +731,7 @@ static cmol_err_t prepare_request(cmol_session_t *s, const int32_t *prompt, int 
     r.prompt.assign(prompt, prompt + n_prompt);
     r.params = *params;
     r.max_new = params->max_new_tokens < 0 ? m->cfg.max_ctx : params->max_new_tokens;
+    r.budget = std::min<long long>((long long)n_prompt + r.max_new, m->cfg.max_ctx - s->n_tokens);
     return CMOL_OK;
 }
 
@@ -742,6 +771,7 @@ extern "C" cmol_err_t cmol_forward_logits(cmol_session_t *s, int32_t token, floa
     r.prompt.assign(1, token);
     r.forward_only = true;
     r.logits_out = logits_out;
+    r.budget = 1;
     return submit_and_wait(s, r, nullptr, nullptr, nullptr);
 }
 
@@ -769,11 +799,15 @@ extern "C" cmol_err_t cmol_forward_logits_batch(cmol_session_t *const *ss, const
         r.prompt.assign(1, tokens[i]);
         r.forward_only = true;
         r.logits_out = logits_out + (size_t)i * m->vocab;
+        r.budget = 1;
     }
     {
         // one hand-over: the worker takes all of them into the same step
         std::lock_guard<std::mutex> lk(w->mu);
-        for (auto &r : rs) w->incoming.push_back(r.get());
+        for (auto &r : rs) {
+            w->load += r->budget;
+            w->incoming.push_back(r.get());
+        }
     }
     w->cv.notify_all();
     cmol_err_t st = CMOL_OK;
@@ -815,7 +849,10 @@ extern "C" cmol_err_t cmol_generate_batch(cmol_batch_item_t *items, int n) {
             for (int i = 0; i < n; i++) {
                 if (!rs[(size_t)i]) continue;
                 cmol_session_t *s = items[i].session;
-                if (s->model->workers[(size_t)s->gpu].get() == w) w->incoming.push_back(rs[(size_t)i].get());
+                if (s->model->workers[(size_t)s->gpu].get() == w) {
+                    w->load += rs[(size_t)i]->budget;
+                    w->incoming.push_back(rs[(size_t)i].get());
+                }
             }
         }
         w->cv.notify_all();
