@@ -196,7 +196,8 @@ def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
     ctx = int(plen.max()) + W + K + 8
     greedy = lambda k: GenParams.make(0.0, repeat_penalty=1.0, max_new_tokens=k)   # noqa: E731
     t_load = time.perf_counter()
-    with Model(path, max_ctx=ctx, max_sessions=sessions, devices=[local], kv_dtype=args.kv) as m:
+    with Model(path, max_ctx=ctx, max_sessions=sessions, devices=[local], kv_dtype=args.kv,
+               page_tokens=args.page_tokens) as m:
         t_load = time.perf_counter() - t_load
         ss = [m.acquire() for _ in range(sessions)]
         # untimed: prefill of every prompt (batched, one sampled token each), then W decode steps
@@ -278,6 +279,7 @@ def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
         "config": {"workload": wl["label"] + (f" (PROFILING: {args.layers} layers)" if args.layers else ""),
                    "model": spec.name, "sessions": int(ses_all),
                    "sessions_per_gpu": sessions, "kv_cache": kv_format_name(args.kv),
+                   "kv_page_tokens": args.page_tokens or 16,
                    "mean_context_timed": round(ctx_sum / max(1, ses_all) + K / 2, 1),
                    "decode_steps_timed": int(steps_max),
                    "l2": "each step reads every weight and every session's KV (GBs), far above the 126 MB L2"},
@@ -825,6 +827,7 @@ def main():
                          "within the 2e-2 / 0.9999 parity tolerance, tests/test_kv_f16_gpu.py)")
     ap.add_argument("--no-nested", action="store_true", help="skip the nested config-2 single-session line")
     ap.add_argument("--layers", type=int, default=0, help="c4: reduced model depth (profiling captures only)")
+    ap.add_argument("--page-tokens", type=int, default=0, help="c4: KV page size in tokens (0: the engine default)")
     ap.add_argument("--profile-timed", action="store_true",
                     help="c4: cudaProfilerStart/Stop around the timed steps (ncu --profile-from-start off)")
     ap.add_argument("--ref-steps", type=int, default=24)

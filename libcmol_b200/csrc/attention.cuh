@@ -22,8 +22,8 @@ struct AttnArgs {
     const int   *slot;       // [ncol] -> page-table row
     const int   *page_table; // [slots][max_pages]
     int          max_pages;
-    const void  *kv_pages;       // f32 values, or f16 when kv_f16
-    long long    page_elems;     // K/V values per page
+    const void  *kv_pages;       // this layer's region of the pool: f32 values, or f16 when kv_f16
+    long long    page_elems;     // K/V values of one page in one layer: [K|V][kv head][token][d_head]
     int          n_pages;        // pages in the pool (bounds check)
     int          kv_f16;         // 1: the pool holds f16 values
     unsigned int *fault;         // device fault word

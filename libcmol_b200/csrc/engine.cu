@@ -344,14 +344,19 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     const int P = o.page_tokens;
     e->max_pages_ = (o.max_ctx + P - 1) / P;
     const int kvb = o.kv_f16 ? 2 : 4;
-    d->page_elems = (long long)L * 2 * nkv * P * hd;
+    // The pool is one region per layer: layer l's K and V of page pg start at
+    // kv_pages + (l * n_pages + pg) * page_elems values, so a layer's pass over
+    // the sessions' contexts stays inside 1 / L of the pool (fewer distinct
+    // memory pages, hence fewer address-translation misses, than pages that
+    // hold every layer).
+    d->page_elems = (long long)2 * nkv * P * hd;
     e->kv_bytes_per_token_ = (long long)L * 2 * KVD * kvb;
     d->page_table = b.dalloc<int>((size_t)o.max_slots * e->max_pages_);
     if (!d->page_table) return fail(-1);
     {
         size_t fr = 0, tot = 0;
         cudaMemGetInfo(&fr, &tot);
-        const size_t page_bytes = (size_t)d->page_elems * kvb;
+        const size_t page_bytes = (size_t)L * d->page_elems * kvb;     // a page of every layer
         long long want = (long long)o.max_slots * e->max_pages_;
         long long fit = (long long)((double)fr * o.kv_pool_frac / (double)page_bytes);
         long long n = want < fit ? want : fit;
@@ -441,6 +446,11 @@ static cudaError_t step_matmul(Engine::Impl *d, const GemvArgs &a, int ncol, int
     return gemv_launch_cols(a, ncol, epi, st, pdl);
 }
 
+// Layer l's region of the KV pool.
+static void *kv_layer(const Engine::Impl *d, int l, const EngineOptions &o) {
+    return static_cast<unsigned char *>(d->kv_pages) + (size_t)l * d->n_pages * d->page_elems * (o.kv_f16 ? 2 : 4);
+}
+
 // What record_step records: the whole step, only its weight products, or
 // only its attention launches (the last two for the kernel sweeps).
 enum { REC_FULL = 0, REC_MATMUL = 1, REC_ATTN = 2 };
@@ -487,7 +497,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         q.d_model = D; q.kv_dim = KVD; q.d_head = hd; q.n_kv = nkv; q.page_tokens = o.page_tokens;
         q.layer = l; q.rope = nope ? 0 : 1; q.rope_cs = d->rope_cs;
         q.pos = d->meta.pos; q.slot = d->meta.slot; q.page_table = d->page_table; q.max_pages = max_pages;
-        q.kv_pages = d->kv_pages; q.page_elems = d->page_elems; q.n_pages = (int)d->n_pages;
+        q.kv_pages = kv_layer(d, l, o); q.page_elems = d->page_elems; q.n_pages = (int)d->n_pages;
         q.kv_f16 = o.kv_f16 ? 1 : 0;
         auto qkv_part = [&](const DevWeight &w, int row_base) -> cudaError_t {
             GemvArgs a = g;
@@ -526,7 +536,7 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
         at.out = d->attn; at.out_ld = D;
         at.pos = d->meta.pos; at.slot = d->meta.slot;
         at.page_table = d->page_table; at.max_pages = max_pages;
-        at.kv_pages = d->kv_pages; at.page_elems = d->page_elems; at.n_pages = (int)d->n_pages;
+        at.kv_pages = kv_layer(d, l, o); at.page_elems = d->page_elems; at.n_pages = (int)d->n_pages;
         at.kv_f16 = o.kv_f16 ? 1 : 0;
         at.fault = d->fault;
         at.layer = l; at.n_heads = hp.n_heads; at.n_kv = nkv; at.d_head = hd; at.page_tokens = o.page_tokens;

@@ -3,6 +3,7 @@
 #include "gemv_launch.cuh"
 
 #include <cuda.h>        // CUtensorMap (the encode call is reached through the runtime)
+#include <stdio.h>
 #include <stdlib.h>
 
 #include <algorithm>
@@ -619,6 +620,16 @@ static void tc_rings(int dt, int npad, int &depth, int &bdepth, int &qdepth, siz
     const size_t qb = (size_t)tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
     const size_t a_slot = (size_t)TC_M * 128, b_slot = (size_t)npad * 128;
     auto need = [&](int da, int db, int dq) { return 1024 + da * a_slot + db * b_slot + dq * qb + bars; };
+    // CMOLCU_TC_RINGS="A,B,Q": ring depths for steps of more than 64 columns
+    // (measurements), used when they fit one CTA per SM
+    static const char *rings = getenv("CMOLCU_TC_RINGS");
+    int fa = 0, fb = 0, fq = 0;
+    if (rings && npad > 64 && sscanf(rings, "%d,%d,%d", &fa, &fb, &fq) == 3 && fa >= 2 && fa <= TC_MAX_DEPTH &&
+        fb >= 2 && fb <= TC_MAX_DEPTH && fq >= 2 && fq <= TC_MAX_QD && need(fa, fb, fq) <= 220 * 1024) {
+        depth = fa; bdepth = fb; qdepth = fq; per_sm = 1;
+        smem = need(fa, fb, fq);
+        return;
+    }
     for (per_sm = max_per_sm; per_sm >= 1; per_sm--) {
         const size_t budget = per_sm == 2 ? 112 * 1024 : 220 * 1024;
         depth = bdepth = qdepth = 2;

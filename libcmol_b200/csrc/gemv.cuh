@@ -52,8 +52,8 @@ struct EpiQKV {
     const int   *slot;          // [ncol] session slot -> page-table row
     const int   *page_table;    // [slots][max_pages]
     int          max_pages;
-    void        *kv_pages;      // page pool (f32, or f16 when kv_f16)
-    long long    page_elems;    // K/V values per page
+    void        *kv_pages;      // this layer's region of the page pool (f32, or f16 when kv_f16)
+    long long    page_elems;    // K/V values of one page in one layer: [K|V][kv head][token][d_head]
     int          n_pages;       // pages in the pool (bounds check)
     int          kv_f16;        // 1: values stored rounded to f16 (nearest, ties to even), chunks
                                 //    swizzled by position (kv_swz)
@@ -337,7 +337,7 @@ __device__ __forceinline__ void epi_qkv_apply(const GemvArgs &a, int lrow, int c
     }
     const int t = pos % e.page_tokens;
     kv_store_pair(e, (long long)pg * e.page_elems +
-                         ((((long long)e.layer * 2 + (is_v ? 1 : 0)) * e.n_kv + head) * e.page_tokens + t) * hd +
+                         (((long long)(is_v ? 1 : 0) * e.n_kv + head) * e.page_tokens + t) * hd +
                          (e.kv_f16 ? kv_swz(pos, dim, hd) : dim),
                   v0, v1);
 }

@@ -132,7 +132,7 @@ __global__ void k_qknorm(QkNormArgs a, int n_heads) {
     const int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
     if (pg < 0 || pg >= e.n_pages) return;
     const int t = pos % e.page_tokens;
-    const long long ko = (long long)pg * e.page_elems + ((((long long)e.layer * 2) * e.n_kv + kh) * e.page_tokens + t) * hd;
+    const long long ko = (long long)pg * e.page_elems + ((long long)kh * e.page_tokens + t) * hd;
     const long long vo = ko + (long long)e.n_kv * e.page_tokens * hd;     // the V block follows the K blocks
     const float *vsrc = a.qkv + (long long)col * a.qkv_ld + D + KVD + kh * hd;
     for (int i = 0; i < hd / 32; i++) {

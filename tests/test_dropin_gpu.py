@@ -34,8 +34,9 @@ def workdir(tmp_path_factory):
 
 
 def _run(args, cwd):
-    r = subprocess.run(args, cwd=cwd, capture_output=True, text=True, timeout=600)
-    return r.returncode, r.stdout + r.stderr
+    r = subprocess.run(args, cwd=cwd, capture_output=True, timeout=600)
+    out = (r.stdout + r.stderr).decode("utf-8", "replace")   # generated text is arbitrary bytes
+    return r.returncode, out
 
 
 @pytest.mark.gpu
