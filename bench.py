@@ -279,7 +279,7 @@ def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
         "config": {"workload": wl["label"] + (f" (PROFILING: {args.layers} layers)" if args.layers else ""),
                    "model": spec.name, "sessions": int(ses_all),
                    "sessions_per_gpu": sessions, "kv_cache": kv_format_name(args.kv),
-                   "kv_page_tokens": args.page_tokens or 16,
+                   "kv_page_tokens": args.page_tokens or 64,
                    "mean_context_timed": round(ctx_sum / max(1, ses_all) + K / 2, 1),
                    "decode_steps_timed": int(steps_max),
                    "l2": "each step reads every weight and every session's KV (GBs), far above the 126 MB L2"},

@@ -23,7 +23,9 @@ extern "C" {
 cmol_err_t cmol_cuda_set_devices(const int *devices, int n);
 
 /* Engine knobs for the next cmol_load (0 keeps the default).
- *   kv_page_tokens : tokens per KV page (default 16)
+ *   kv_page_tokens : tokens per KV page (default 64: one kv head's K and V of a
+ *                    page form one contiguous block, which attention reads
+ *                    at full HBM rate; much smaller pages read far slower)
  *   kv_pool_frac   : fraction of free device memory the KV pool may take
  *                    when the full max_sessions * max_ctx does not fit
  *                    (default 0.85)

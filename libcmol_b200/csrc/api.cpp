@@ -265,7 +265,7 @@ extern "C" cmol_model_t *cmol_load(const char *path, const cmol_config_t *cfg, c
             eo.max_batch = (opt.max_batch > 0 ? std::min(opt.max_batch, per_gpu) : per_gpu) + (prefill > 1 ? prefill : 0);
             eo.max_group = prefill;
             eo.max_ctx = m->cfg.max_ctx;
-            eo.page_tokens = opt.kv_page_tokens > 0 ? opt.kv_page_tokens : 16;
+            eo.page_tokens = opt.kv_page_tokens > 0 ? opt.kv_page_tokens : 64;
             eo.kv_pool_frac = opt.kv_pool_frac > 0.f ? opt.kv_pool_frac : 0.85f;
             eo.use_graphs = opt.use_graphs != 0;
             eo.kv_f16 = opt.kv_dtype == 1;

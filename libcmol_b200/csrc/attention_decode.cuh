@@ -126,8 +126,8 @@ __device__ __forceinline__ bool dec_issue(const AttnArgs &a, const int *pt, int 
             return false;
         }
     }
-    const long long head_off = (long long)blockIdx.y * P * hd;    // the kv head's K block in the page
-    const long long v_off = (long long)a.n_kv * P * hd;
+    const long long head_off = (long long)blockIdx.y * 2 * P * hd;    // the kv head's K block in the page
+    const long long v_off = (long long)P * hd;
     const unsigned char *pool = static_cast<const unsigned char *>(a.kv_pages);
     const uint32_t blk = (uint32_t)(P * hd * KB);
     mbar_arrive_expect_tx(bar, 2u * npg * blk);
@@ -526,8 +526,8 @@ __global__ void __launch_bounds__(PERS_THREADS, 1) k_attn_pers(AttnArgs a, int s
             if (lane == 0) {
                 nxt = *vfail ? total : atomicAdd(&work[0], 1);   // in flight while this item streams
                 const uint32_t blk = (uint32_t)(P * hd * 2);
-                const long long head_off = (long long)hk * P * hd;
-                const long long v_off = (long long)nkv * P * hd;
+                const long long head_off = (long long)hk * 2 * P * hd;
+                const long long v_off = (long long)P * hd;
                 const unsigned char *pool = static_cast<const unsigned char *>(a.kv_pages);
                 for (int j = 0; j < nsub; j++, k++) {
                     const int st = k % stages;

@@ -79,8 +79,8 @@ __device__ bool attn_item(const AttnArgs &a, int s, int hk, int col, int pos, co
     if (t0 > pos) return true;
     const int n = min(S, pos + 1 - t0);                       // tokens in this split
     const int n_active = (pos + S) / S;
-    const long long head_off = (long long)hk * P * hd;   // the kv head's K block in the layer's page
-    const long long v_off = (long long)a.n_kv * P * hd;                            // V block follows
+    const long long head_off = (long long)hk * 2 * P * hd;   // the kv head's K block in the layer's page
+    const long long v_off = (long long)P * hd;                            // V block follows
 
     if (tid == 0) {
         int ok = 1;
@@ -305,8 +305,8 @@ __device__ bool attn_group_item(const AttnArgs &a, int s, int hk, int c, int pos
     float *Wsum = Wmax + QC * G;                                          // [QC][G]
     int *Merge = reinterpret_cast<int *>(Wsum + QC * G);                  // [QC]
     const int *pt = a.page_table + (long long)slot_c * a.max_pages;
-    const long long head_off = (long long)hk * P * hd;
-    const long long v_off = (long long)a.n_kv * P * hd;
+    const long long head_off = (long long)hk * 2 * P * hd;
+    const long long v_off = (long long)P * hd;
 
     if (tid == 0) {
         int ok = 1;

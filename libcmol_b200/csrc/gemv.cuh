@@ -337,7 +337,7 @@ __device__ __forceinline__ void epi_qkv_apply(const GemvArgs &a, int lrow, int c
     }
     const int t = pos % e.page_tokens;
     kv_store_pair(e, (long long)pg * e.page_elems +
-                         (((long long)(is_v ? 1 : 0) * e.n_kv + head) * e.page_tokens + t) * hd +
+                         (((long long)head * 2 + (is_v ? 1 : 0)) * e.page_tokens + t) * hd +
                          (e.kv_f16 ? kv_swz(pos, dim, hd) : dim),
                   v0, v1);
 }

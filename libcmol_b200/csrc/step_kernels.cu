@@ -132,8 +132,8 @@ __global__ void k_qknorm(QkNormArgs a, int n_heads) {
     const int pg = e.page_table[(long long)srow * e.max_pages + pos / e.page_tokens];
     if (pg < 0 || pg >= e.n_pages) return;
     const int t = pos % e.page_tokens;
-    const long long ko = (long long)pg * e.page_elems + ((long long)kh * e.page_tokens + t) * hd;
-    const long long vo = ko + (long long)e.n_kv * e.page_tokens * hd;     // the V block follows the K blocks
+    const long long ko = (long long)pg * e.page_elems + ((long long)kh * 2 * e.page_tokens + t) * hd;
+    const long long vo = ko + (long long)e.page_tokens * hd;     // the head's V block follows its K block
     const float *vsrc = a.qkv + (long long)col * a.qkv_ld + D + KVD + kh * hd;
     for (int i = 0; i < hd / 32; i++) {
         const int j = lane + 32 * i;
