@@ -137,6 +137,8 @@ struct TcParams {
     int             qdepth;            // quantised-stage ring depth (<= TC_MAX_QD)
     int             cluster;           // 1: the K splits of a row block form one cluster and add
                                        // their partials through distributed shared memory
+    int             msub;              // 128-row sub-tiles per CTA (1, or 2: two TMEM accumulators
+                                       // share every activation tile; no K split then)
 };
 
 // A quantised stage holds one 256-value slice of 128 rows, loaded by TMA
@@ -373,18 +375,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     const QWeight &w = p.g.w;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rb = blockIdx.x, ks = blockIdx.y;
-    const int m0 = rb * TC_M;
+    const int MS = p.msub;
+    const int m0 = rb * TC_M * MS;
     const int npad = p.npad;
     const int s0 = ks * p.slices_per_split, s1 = min(p.nslice, s0 + p.slices_per_split);
-    constexpr int QB = tc_stage_bytes(DT);
+    constexpr int QB = tc_stage_bytes(DT);                   // one 128-row sub-tile of a slice
 
     // shared memory: A tiles, B tiles (1024-aligned), quantised stages, barriers
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
     const int D = p.depth, DB = p.bdepth, QD = p.qdepth;
-    uint8_t *A = base;                                        // D x 16 KB
-    uint8_t *B = A + (size_t)D * TC_M * 128;                  // DB x npad * 128
-    uint8_t *Q = B + (size_t)DB * npad * 128;                 // QD x QB
-    uint64_t *bars = reinterpret_cast<uint64_t *>(Q + (size_t)QD * QB);
+    uint8_t *A = base;                                        // D x MS x 16 KB
+    uint8_t *B = A + (size_t)D * MS * TC_M * 128;             // DB x npad * 128
+    uint8_t *Q = B + (size_t)DB * npad * 128;                 // QD x MS x QB
+    uint64_t *bars = reinterpret_cast<uint64_t *>(Q + (size_t)QD * MS * QB);
     uint64_t *accfull = bars, *qfull = bars + 1, *qempty = qfull + TC_MAX_QD, *afull = qempty + TC_MAX_QD,
              *aempty = afull + TC_MAX_DEPTH, *bfull = aempty + TC_MAX_DEPTH, *bempty = bfull + TC_MAX_DEPTH;
     __shared__ uint32_t s_tmem;
@@ -446,14 +449,18 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                 const bool last = j == w.nkc - 1;
                 const CUtensorMap *mp = last ? p.tm_last : p.tm_full;
                 const int z = last ? 0 : j;
-                uint8_t *q = Q + (size_t)stg * QB;
                 const int o0 = qw_plane_bytes(DT, 0, off), o1 = qw_plane_bytes(DT, 1, off);
-                mbar_arrive_expect_tx(&qfull[stg], (uint32_t)tc_stage_tx(DT));
+                mbar_arrive_expect_tx(&qfull[stg], (uint32_t)(MS * tc_stage_tx(DT)));
+                for (int sb = 0; sb < MS; sb++) {
+                    uint8_t *q = Q + ((size_t)stg * MS + sb) * QB;
+                    const int my = m0 + TC_M * sb;
 #pragma unroll
-                for (int b = 0; b < tc_nb0(DT); b++) tma_load_3d(q + b * TC_M * 128, &mp[0], o0 + 128 * b, m0, z, &qfull[stg]);
-                tma_load_3d(q + tc_off1(DT), &mp[1], o1, m0, z, &qfull[stg]);
-                if constexpr (DT == DT_Q5_0)
-                    tma_load_3d(q + tc_off2(DT), &mp[2], qw_plane_bytes(DT, 2, off), m0, z, &qfull[stg]);
+                    for (int b = 0; b < tc_nb0(DT); b++)
+                        tma_load_3d(q + b * TC_M * 128, &mp[0], o0 + 128 * b, my, z, &qfull[stg]);
+                    tma_load_3d(q + tc_off1(DT), &mp[1], o1, my, z, &qfull[stg]);
+                    if constexpr (DT == DT_Q5_0)
+                        tma_load_3d(q + tc_off2(DT), &mp[2], qw_plane_bytes(DT, 2, off), my, z, &qfull[stg]);
+                }
             }
         }
     } else if (warp == 2) {
@@ -484,10 +491,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                 mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
                 mbar_wait(&bfull[bslot], buse & 1, p.g.fault, FAULT_GEMV_FULL);
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(A + slot * TC_M * 128), b_addr = smem_u32(B + (size_t)bslot * npad * 128);
+                const uint32_t a_addr = smem_u32(A + (size_t)slot * MS * TC_M * 128);
+                const uint32_t b_addr = smem_u32(B + (size_t)bslot * npad * 128);
+                for (int sb = 0; sb < MS; sb++)          // sub-tile sb accumulates at columns [sb * npad, ...)
 #pragma unroll
-                for (int k = 0; k < TC_KB / 16; k++)
-                    tc_mma(tmem, tc_desc(a_addr + 32 * k), tc_desc(b_addr + 32 * k), idesc, (i | k) != 0);
+                    for (int k = 0; k < TC_KB / 16; k++)
+                        tc_mma(tmem + (uint32_t)(sb * npad), tc_desc(a_addr + sb * TC_M * 128 + 32 * k),
+                               tc_desc(b_addr + 32 * k), idesc, (i | k) != 0);
                 tc_commit(&aempty[slot]);
                 tc_commit(&bempty[bslot]);
             }
@@ -502,14 +512,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
             mbar_wait(&qfull[stg], (li / QD) & 1, p.g.fault, FAULT_GEMV_FULL);
             int j, off, len;
             tc_slice(w, t, j, off, len);
-            const uint8_t *q = Q + (size_t)stg * QB;
             for (int ib = 0; ib < len / TC_KB; ib++, i++) {
                 const int slot = i % D, use = i / D;
                 if (use > 0) mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY);
-                uint8_t *tile = A + slot * TC_M * 128;
-                // task = (row r, 32-value half hf): 128 rows x 2 halves, one per thread
+                // task = (row r, 32-value half hf): 128 rows x 2 halves a sub-tile, one per thread
                 static_assert(TC_M * 2 == TC_DQT, "one 32-value task per dequantising thread");
-                {
+                for (int sb = 0; sb < MS; sb++) {
+                    const uint8_t *q = Q + ((size_t)stg * MS + sb) * QB;
+                    uint8_t *tile = A + ((size_t)slot * MS + sb) * TC_M * 128;
                     const int r = dt >> 1, hf = dt & 1;
                     uint32_t h[16];
                     tc_dequant32<DT>(q, r, ib * TC_KB + 32 * hf, h);
@@ -526,15 +536,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
             if (lane == 0) mbar_arrive(&qempty[stg]);
         }
         // ---------------- epilogue: tensor memory -> registers ----------------
-        if (warp < 7) {
-            const int quarter = warp & 3;                 // the TMEM lanes this warp may read (warps 3..6)
-            const int row = m0 + 32 * quarter + lane;
+        // The 8 dequantising warps: warp w reads TMEM lanes 32 * (w % 4) ..;
+        // warps 3-6 and 7-10 take the two sub-tiles (MS = 2) or the two
+        // halves of the columns (MS = 1).
+        {
+            const int ew = warp - 3, quarter = warp & 3, grp = ew >> 2;
+            const int sb = MS == 2 ? grp : 0;
+            const int ch = npad >= 32 ? (npad / 32) * 16 : npad;    // column split of MS = 1 (16-column units)
+            const int c_lo = MS == 2 ? 0 : (grp ? ch : 0), c_hi = MS == 2 ? npad : (grp ? npad : ch);
+            const int row = m0 + TC_M * sb + 32 * quarter + lane;
             mbar_wait(accfull, 0, p.g.fault, FAULT_GEMV_FULL);
             tc_fence_after();
             if (p.ksplit == 1) pdl_wait();
-            for (int c0 = 0; c0 < npad; c0 += 16) {
+            for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                 float v[16];
-                tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, v);
+                tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(sb * npad + c0), v);
                 if (p.ksplit == 1) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
@@ -615,10 +631,10 @@ static int tc_knob(const char *name, int dflt) {
 // SM.  Spare room deepens, in this order: the activation ring (its tiles
 // are small at narrow batches, and a shallow one puts an L2 round trip
 // behind every k-block's MMA), the dequantised ring, the quantised ring.
-static void tc_rings(int dt, int npad, int &depth, int &bdepth, int &qdepth, size_t &smem, int &per_sm) {
+static void tc_rings(int dt, int npad, int ms, int &depth, int &bdepth, int &qdepth, size_t &smem, int &per_sm) {
     static const int max_per_sm = tc_knob("CMOLCU_TC_PER_SM", 2) == 1 ? 1 : 2;
-    const size_t qb = (size_t)tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
-    const size_t a_slot = (size_t)TC_M * 128, b_slot = (size_t)npad * 128;
+    const size_t qb = (size_t)ms * tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
+    const size_t a_slot = (size_t)ms * TC_M * 128, b_slot = (size_t)npad * 128;
     auto need = [&](int da, int db, int dq) { return 1024 + da * a_slot + db * b_slot + dq * qb + bars; };
     // CMOLCU_TC_RINGS="A,B,Q": ring depths for steps of more than 64 columns
     // (measurements), used when they fit one CTA per SM
@@ -657,11 +673,11 @@ static int tc_nslice(int k, int kc) {
     return (nkc - 1) * (kc / TC_SV) + (last + TC_SV - 1) / TC_SV;
 }
 
-static void tc_split(int rows, int nslice, int per_sm, int &rblocks, int &ksplit, int &sps) {
+static void tc_split(int rows, int nslice, int per_sm, int ms, int &rblocks, int &ksplit, int &sps) {
     static const int cap = std::max(1, tc_knob("CMOLCU_TC_KSPLIT_MAX", 1 << 20));
     const int slots = device_sm_count() * per_sm;
-    rblocks = (rows + TC_M - 1) / TC_M;
-    ksplit = std::max(1, std::min(std::min(nslice, cap), slots / rblocks));    // one wave
+    rblocks = (rows + TC_M * ms - 1) / (TC_M * ms);
+    ksplit = ms > 1 ? 1 : std::max(1, std::min(std::min(nslice, cap), slots / rblocks));    // one wave
     sps = (nslice + ksplit - 1) / ksplit;
     ksplit = (nslice + sps - 1) / sps;
 }
@@ -670,7 +686,7 @@ void tc_scratch_need(int rows, int k, int ncol, size_t *xs_halves, size_t *part_
     const int npad = tc_npad(ncol);
     *xs_halves = (size_t)k * npad;
     int rb, ks, sps;
-    tc_split(rows, k / TC_KB, 2, rb, ks, sps);     // an upper bound on the split of any format
+    tc_split(rows, k / TC_KB, 2, 1, rb, ks, sps);     // an upper bound on the split of any format
     *part_floats = ks > 1 ? (size_t)rb * ks * npad * TC_M : 0;
     *row_blocks = rb;
 }
@@ -804,12 +820,23 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     if (w.nkc > 1 && w.kc % TC_SV) return cudaErrorInvalidValue;
     if (w.dtype == DT_Q4_K && w.k % TC_SV) return cudaErrorInvalidValue;
     const int npad = tc_npad(ncol);
+    // Two 128-row sub-tiles per CTA (both accumulators reuse every activation
+    // tile, halving its shared-memory ingest per output row) for wide steps
+    // on matrices with rows for well over half a wave of such CTAs, when the
+    // rings still fit (not Q8_0, whose slices are twice as large).
+    static const int ms_knob = tc_knob("CMOLCU_TC_MSUB", 0);
+    int ms = (npad >= 128 && w.rows >= 2 * TC_M * 64 && w.dtype != DT_Q8_0) ? 2 : 1;
+    if (ms_knob == 1 || ms_knob == 2) ms = ms_knob;
     int depth, bdepth, qdepth, per_sm;
     size_t smem;
-    tc_rings(w.dtype, npad, depth, bdepth, qdepth, smem, per_sm);
+    tc_rings(w.dtype, npad, ms, depth, bdepth, qdepth, smem, per_sm);
+    if (ms == 2 && smem > 220 * 1024) {
+        ms = 1;
+        tc_rings(w.dtype, npad, ms, depth, bdepth, qdepth, smem, per_sm);
+    }
     const int nslice = tc_nslice(w.k, w.kc);
     int rb, ks, sps;
-    tc_split(w.rows, nslice, per_sm, rb, ks, sps);
+    tc_split(w.rows, nslice, per_sm, ms, rb, ks, sps);
     if (!s.xs || rb > s.max_row_blocks || (ks > 1 && (size_t)rb * ks * npad * TC_M > s.part_floats))
         return cudaErrorInvalidValue;
     TcParams p = {};
@@ -824,7 +851,9 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     p.slices_per_split = sps;
     p.part = s.part;
     p.counters = s.counters;
-    p.tmem_cols = npad <= 32 ? 32 : npad <= 64 ? 64 : npad <= 128 ? 128 : 256;
+    p.msub = ms;
+    const int tcols = ms * npad;
+    p.tmem_cols = tcols <= 32 ? 32 : tcols <= 64 ? 64 : tcols <= 128 ? 128 : tcols <= 256 ? 256 : 512;
     p.depth = depth;
     p.bdepth = bdepth;
     p.qdepth = qdepth;
@@ -849,7 +878,8 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     if (smem > attr_done[dev][di]) return cudaErrorInvalidConfiguration;
     // split partials through distributed shared memory when the splits fit in
     // one cluster and a partial ([npad][128] floats) fits in the drained rings
-    const size_t rings = (size_t)depth * TC_M * 128 + (size_t)bdepth * npad * 128 + (size_t)qdepth * tc_stage_bytes(w.dtype);
+    const size_t rings = (size_t)depth * ms * TC_M * 128 + (size_t)bdepth * npad * 128 +
+                         (size_t)qdepth * ms * tc_stage_bytes(w.dtype);
     static const bool no_cluster = tc_knob("CMOLCU_TC_CLUSTER", 1) == 0;
     p.cluster = !no_cluster && ks > 1 && (size_t)npad * TC_M * 4 <= rings && tc_cluster_ok(k, ks, rb, smem) ? 1 : 0;
     cudaError_t e = launch_k(k_tc_xprep, dim3(npad), dim3(256), 0, st, pdl, a.x, a.x_ld, w.k, ncol, npad, a.norm_w,

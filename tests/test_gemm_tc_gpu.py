@@ -22,6 +22,11 @@ CASES = [
     (synth.Q5_0, 512, 2048, 64),
     (synth.Q8_0, 19200, 512, 16),     # > 148 row blocks: no K split, epilogue from tensor memory
     (synth.Q4_K, 1024, 4096, 256),    # the widest column count
+    # >= 64 blocks of 256 rows at 128+ columns: two 128-row sub-tiles per CTA
+    # (two tensor-memory accumulators share each activation tile); the last
+    # block is ragged (a partial second sub-tile)
+    (synth.Q4_K, 16512, 512, 256),
+    (synth.Q4_0, 16448, 256, 130),
 ]
 
 
