@@ -392,6 +392,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
              *aempty = afull + TC_MAX_DEPTH, *bfull = aempty + TC_MAX_DEPTH, *bempty = bfull + TC_MAX_DEPTH;
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
+    // Set when a bounded wait of any role ran out (the fault word holds the
+    // code): no role starts new copies or products after it, and each
+    // producer waits for the copies it has issued before the CTA tears down.
+    __shared__ int s_abort;
+    volatile int *abort_flag = &s_abort;
 
     if (tid == 0) {
         // the weight's tensor maps, fetched while the rest of the setup runs
@@ -415,6 +420,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         }
         mbar_init(accfull, 1);
         fence_mbar_init();
+        s_abort = 0;
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -441,9 +447,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         // gated only by the dequantising warps releasing stages, so the ring
         // runs QD slices ahead of the dequantisation
         if (lane == 0) {
+            int issued = 0;
             for (int t = s0; t < s1; t++) {
                 const int li = t - s0, stg = li % QD, use = li / QD;
-                if (use > 0 && !mbar_wait(&qempty[stg], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) break;
+                if (*abort_flag) break;
+                if (use > 0 && !mbar_wait(&qempty[stg], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) {
+                    *abort_flag = 1;
+                    break;
+                }
                 int j, off, len;
                 tc_slice(w, t, j, off, len);
                 const bool last = j == w.nkc - 1;
@@ -461,7 +472,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                     if constexpr (DT == DT_Q5_0)
                         tma_load_3d(q + tc_off2(DT), &mp[2], qw_plane_bytes(DT, 2, off), my, z, &qfull[stg]);
                 }
+                issued = li + 1;
             }
+            // the last QD slices issued have landed before the CTA goes on
+            // (immediately true for the ones the dequantisation consumed)
+            for (int li = issued - 1; li >= 0 && li >= issued - QD; li--)
+                mbar_wait(&qfull[li % QD], (li / QD) & 1, nullptr, 0);
         }
     } else if (warp == 2) {
         // ---------------- activation producer: one k-block of the image per tile slot ----------------
@@ -475,12 +491,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                 const int g0 = (j * w.kc + off) / TC_KB;
                 for (int i = 0; i < len / TC_KB; i++, bn++) {
                     const int slot = bn % DB, u = bn / DB;
-                    if (u > 0 && !mbar_wait(&bempty[slot], (u - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) { ok = false; break; }
+                    if (*abort_flag) { ok = false; break; }
+                    if (u > 0 && !mbar_wait(&bempty[slot], (u - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
                     mbar_arrive_expect_tx(&bfull[slot], (uint32_t)(npad * 128));
                     bulk_g2s(B + (size_t)slot * npad * 128, p.xs + (size_t)(g0 + i) * npad * 64, (uint32_t)(npad * 128),
                              &bfull[slot]);
                 }
             }
+            for (int b = bn - 1; b >= 0 && b >= bn - DB; b--)   // the copies issued have landed
+                mbar_wait(&bfull[b % DB], (b / DB) & 1, nullptr, 0);
         }
     } else if (warp == 1) {
         // ---------------- MMA issue ----------------
@@ -488,8 +511,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
             const uint32_t idesc = (1u << 4) | ((uint32_t)(npad >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
             for (int i = 0; i < nkb; i++) {
                 const int slot = i % D, use = i / D, bslot = i % DB, buse = i / DB;
-                mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL);
-                mbar_wait(&bfull[bslot], buse & 1, p.g.fault, FAULT_GEMV_FULL);
+                if (*abort_flag || !mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL) ||
+                    !mbar_wait(&bfull[bslot], buse & 1, p.g.fault, FAULT_GEMV_FULL)) {
+                    *abort_flag = 1;
+                    break;                              // accfull below still tracks the products issued
+                }
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(A + (size_t)slot * MS * TC_M * 128);
                 const uint32_t b_addr = smem_u32(B + (size_t)bslot * npad * 128);
@@ -507,14 +533,25 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         // ---------------- dequantise ----------------
         const int dt = tid - 96;
         int i = 0;
-        for (int t = s0; t < s1; t++) {
+        bool dq_ok = true;
+        for (int t = s0; t < s1 && dq_ok; t++) {
             const int li = t - s0, stg = li % QD;
-            mbar_wait(&qfull[stg], (li / QD) & 1, p.g.fault, FAULT_GEMV_FULL);
+            // warp-uniform outcome of each wait: the warp leaves its loops together
+            if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&qfull[stg], (li / QD) & 1, p.g.fault,
+                                                                       FAULT_GEMV_FULL))) {
+                *abort_flag = 1;
+                break;
+            }
             int j, off, len;
             tc_slice(w, t, j, off, len);
             for (int ib = 0; ib < len / TC_KB; ib++, i++) {
                 const int slot = i % D, use = i / D;
-                if (use > 0) mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY);
+                if (use > 0 &&
+                    !__all_sync(0xffffffffu, mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY))) {
+                    *abort_flag = 1;
+                    dq_ok = false;
+                    break;
+                }
                 // task = (row r, 32-value half hf): 128 rows x 2 halves a sub-tile, one per thread
                 static_assert(TC_M * 2 == TC_DQT, "one 32-value task per dequantising thread");
                 for (int sb = 0; sb < MS; sb++) {
