@@ -220,8 +220,9 @@ static cudaError_t launch_dec(const AttnArgs &a, int ncol, cudaStream_t st, bool
 
 template <int E>
 static cudaError_t launch_pers(const AttnArgs &a, cudaStream_t st, bool pdl) {
-    const int stages = pers_stages(32 * E, a.max_cols, PERS_SMEM_BUDGET);
-    const size_t smem = pers_fixed_bytes(32 * E, a.max_cols) + (size_t)stages * pers_stage_bytes(32 * E);
+    const int G = a.n_heads / a.n_kv;
+    const int stages = pers_stages(32 * E, G, a.max_cols, PERS_SMEM_BUDGET);
+    const size_t smem = pers_fixed_bytes(32 * E, G, a.max_cols) + (size_t)stages * pers_stage_bytes(32 * E, G);
     static int attr_dev = -1;
     static size_t attr_smem = 0;
     int dev = 0;
@@ -272,7 +273,7 @@ cudaError_t attention_launch(const AttnArgs &a_in, int ncol, cudaStream_t st, bo
         a.chunk_tokens = DEC_SUB * subs;
         const bool h = a.kv_f16 != 0;
         if (h && a.tc_min_cols > 0 && ncol >= a.tc_min_cols && a.order && a.work &&
-            pers_stages(a.d_head, a.max_cols, PERS_SMEM_BUDGET) >= 2)
+            pers_stages(a.d_head, G, a.max_cols, PERS_SMEM_BUDGET) >= 2)
             return a.d_head == 64 ? launch_pers<2>(a, st, pdl) : launch_pers<4>(a, st, pdl);
         if (a.d_head == 64) return h ? launch_dec_g<2, true>(a, ncol, st, pdl) : launch_dec_g<2, false>(a, ncol, st, pdl);
         return h ? launch_dec_g<4, true>(a, ncol, st, pdl) : launch_dec_g<4, false>(a, ncol, st, pdl);

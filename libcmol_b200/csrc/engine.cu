@@ -619,8 +619,8 @@ static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, i
         for (int r = 0; r < nl; r++) t += cols[order[r]].pos / c + 1;
         return t * n_kv;
     };
-    int ch = 4096;                                // at most 1024 pages an item (its page list in shared memory)
-    while (ch > 1024 * page_tokens) ch >>= 1;
+    int ch = 4096;                                // at most 256 pages an item (its page list in shared memory)
+    while (ch > 256 * page_tokens) ch >>= 1;
     while (ch > 64 && items(ch) < target) ch >>= 1;
     pfx[0] = 0;
     for (int r = 0; r < nl; r++) pfx[r + 1] = pfx[r] + cols[order[r]].pos / ch + 1;
