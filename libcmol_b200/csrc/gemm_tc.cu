@@ -14,7 +14,10 @@
 #define TC_THREADS ((3 + TC_DQW) * 32)    // + weight producer warp 0, MMA warp 1, activation producer warp 2
 #define TC_DQT (TC_DQW * 32)
 #define TC_MAX_DEPTH 8
-#define TC_RU 4                           // split-K reduction: tasks per thread in flight
+#define TC_TS_MIN_DEPTH 2                 // dequantised ring in tensor memory: depth range
+#define TC_TS_MAX_DEPTH 4
+#define TC_RU 1                           // split-K reduction: tasks per thread, and
+#define TC_RS 8                           // splits of each, whose loads are in flight together
 
 bool tc_supported(int dt) { return dt == DT_Q4_K || dt == DT_Q8_0 || dt == DT_Q4_0 || dt == DT_Q5_0; }
 
@@ -44,6 +47,29 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db
         "l"(da), "l"(db), "r"(idesc), "r"(acc)
         : "memory");
 }
+
+// The same product with A in tensor memory: row m of A is lane m, and each
+// 32-bit column holds two consecutive K values (lower half first), so a K=16
+// product reads 8 columns from `tmem_a`.
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                          uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t h[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7]), "r"(h[8]), "r"(h[9]),
+        "r"(h[10]), "r"(h[11]), "r"(h[12]), "r"(h[13]), "r"(h[14]), "r"(h[15])
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Arrives on `bar` once every tcgen05 operation this thread issued so far has completed.
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
@@ -139,6 +165,9 @@ struct TcParams {
                                        // their partials through distributed shared memory
     int             msub;              // 128-row sub-tiles per CTA (1, or 2: two TMEM accumulators
                                        // share every activation tile; no K split then)
+    int             ts;                // 1: the dequantised tiles live in tensor memory (columns
+                                       // a_col + (slot * msub + sub-tile) * 32 ..), not shared memory
+    uint32_t        a_col;
 };
 
 // A quantised stage holds one 256-value slice of 128 rows, loaded by TMA
@@ -328,9 +357,11 @@ __device__ __forceinline__ void tc_epilogue(const TcParams &p, int row, int col,
 
 // Adds the split partials of this row block for columns [c_lo, c_hi) and
 // runs the epilogue.  Task = (column, 4 consecutive rows); a thread takes
-// TC_RU tasks at once so that TC_RU float4 loads per split are in flight
-// together.  Partials add in split order (deterministic); the even row of a
-// pair applies pair epilogues.  load(split, column, row quad) -> float4.
+// TC_RU tasks at once and loads TC_RS splits of each before adding any, so
+// TC_RU * TC_RS float4 loads are in flight together (the partials come from
+// other CTAs' shared memory or from L2: latency, not bandwidth, bounds this).
+// Partials add in split order (deterministic); the even row of a pair
+// applies pair epilogues.  load(split, column, row quad) -> float4.
 template <typename LoadF>
 __device__ __forceinline__ void tc_reduce_cols(const TcParams &p, int m0, int c_lo, int c_hi, int tid, LoadF load) {
     constexpr int RQ = TC_M / 4;
@@ -339,17 +370,22 @@ __device__ __forceinline__ void tc_reduce_cols(const TcParams &p, int m0, int c_
         float4 acc[TC_RU];
 #pragma unroll
         for (int u = 0; u < TC_RU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int sp = 0; sp < p.ksplit; sp++) {
-            float4 v[TC_RU];
+        for (int s0 = 0; s0 < p.ksplit; s0 += TC_RS) {
+            float4 v[TC_RU][TC_RS];
 #pragma unroll
             for (int u = 0; u < TC_RU; u++) {
                 const int idx = base + u * TC_THREADS;
-                v[u] = idx < ntask ? load(sp, c_lo + idx / RQ, idx % RQ) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int r = 0; r < TC_RS; r++)
+                    v[u][r] = idx < ntask && s0 + r < p.ksplit ? load(s0 + r, c_lo + idx / RQ, idx % RQ)
+                                                               : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int u = 0; u < TC_RU; u++) {
-                acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
-            }
+            for (int u = 0; u < TC_RU; u++)
+#pragma unroll
+                for (int r = 0; r < TC_RS; r++) {
+                    acc[u].x += v[u][r].x; acc[u].y += v[u][r].y; acc[u].z += v[u][r].z; acc[u].w += v[u][r].w;
+                }
         }
 #pragma unroll
         for (int u = 0; u < TC_RU; u++) {
@@ -384,8 +420,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     // shared memory: A tiles, B tiles (1024-aligned), quantised stages, barriers
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)cmolcu_smem + 1023) & ~(uintptr_t)1023);
     const int D = p.depth, DB = p.bdepth, QD = p.qdepth;
-    uint8_t *A = base;                                        // D x MS x 16 KB
-    uint8_t *B = A + (size_t)D * MS * TC_M * 128;             // DB x npad * 128
+    uint8_t *A = base;                                        // D x MS x 16 KB (none in tensor memory)
+    uint8_t *B = A + (p.ts ? (size_t)0 : (size_t)D * MS * TC_M * 128);   // DB x npad * 128
     uint8_t *Q = B + (size_t)DB * npad * 128;                 // QD x MS x QB
     uint64_t *bars = reinterpret_cast<uint64_t *>(Q + (size_t)QD * MS * QB);
     uint64_t *accfull = bars, *qfull = bars + 1, *qempty = qfull + TC_MAX_QD, *afull = qempty + TC_MAX_QD,
@@ -483,14 +519,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         // ---------------- activation producer: one k-block of the image per tile slot ----------------
         if (lane == 0) {
             pdl_wait();   // the activation image comes from the previous kernel
-            int bn = 0;
+            int bn = 0, slot = 0, u = 0;                // tiles issued; ring slot and its use
             bool ok = true;
             for (int t = s0; t < s1 && ok; t++) {
                 int j, off, len;
                 tc_slice(w, t, j, off, len);
                 const int g0 = (j * w.kc + off) / TC_KB;
-                for (int i = 0; i < len / TC_KB; i++, bn++) {
-                    const int slot = bn % DB, u = bn / DB;
+                for (int i = 0; i < len / TC_KB; i++, bn++, u += ++slot == DB, slot = slot == DB ? 0 : slot) {
                     if (*abort_flag) { ok = false; break; }
                     if (u > 0 && !mbar_wait(&bempty[slot], (u - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY)) {
                         *abort_flag = 1;
@@ -509,8 +544,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
         // ---------------- MMA issue ----------------
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | ((uint32_t)(npad >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
-            for (int i = 0; i < nkb; i++) {
-                const int slot = i % D, use = i / D, bslot = i % DB, buse = i / DB;
+            // ring slots and their parities advance by counting (no division in the loop)
+            int slot = 0, use = 0, bslot = 0, buse = 0;
+            for (int i = 0; i < nkb; i++, use += ++slot == D, slot = slot == D ? 0 : slot,
+                     buse += ++bslot == DB, bslot = bslot == DB ? 0 : bslot) {
                 if (*abort_flag || !mbar_wait(&afull[slot], use & 1, p.g.fault, FAULT_GEMV_FULL) ||
                     !mbar_wait(&bfull[bslot], buse & 1, p.g.fault, FAULT_GEMV_FULL)) {
                     *abort_flag = 1;
@@ -519,11 +556,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(A + (size_t)slot * MS * TC_M * 128);
                 const uint32_t b_addr = smem_u32(B + (size_t)bslot * npad * 128);
-                for (int sb = 0; sb < MS; sb++)          // sub-tile sb accumulates at columns [sb * npad, ...)
+                for (int sb = 0; sb < MS; sb++) {        // sub-tile sb accumulates at columns [sb * npad, ...)
+                    if (p.ts) {
+                        const uint32_t ta = tmem + p.a_col + (uint32_t)((slot * MS + sb) * 32);
 #pragma unroll
-                    for (int k = 0; k < TC_KB / 16; k++)
-                        tc_mma(tmem + (uint32_t)(sb * npad), tc_desc(a_addr + sb * TC_M * 128 + 32 * k),
-                               tc_desc(b_addr + 32 * k), idesc, (i | k) != 0);
+                        for (int k = 0; k < TC_KB / 16; k++)
+                            tc_mma_ts(tmem + (uint32_t)(sb * npad), ta + 8 * k, tc_desc(b_addr + 32 * k), idesc,
+                                      (i | k) != 0);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < TC_KB / 16; k++)
+                            tc_mma(tmem + (uint32_t)(sb * npad), tc_desc(a_addr + sb * TC_M * 128 + 32 * k),
+                                   tc_desc(b_addr + 32 * k), idesc, (i | k) != 0);
+                    }
+                }
                 tc_commit(&aempty[slot]);
                 tc_commit(&bempty[bslot]);
             }
@@ -532,28 +578,44 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
     } else {
         // ---------------- dequantise ----------------
         const int dt = tid - 96;
-        int i = 0;
+        int i = 0, slot = 0, use = 0;                   // k-blocks done; A ring slot and its use
         bool dq_ok = true;
         for (int t = s0; t < s1 && dq_ok; t++) {
             const int li = t - s0, stg = li % QD;
             // warp-uniform outcome of each wait: the warp leaves its loops together
             if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait(&qfull[stg], (li / QD) & 1, p.g.fault,
-                                                                       FAULT_GEMV_FULL))) {
+                                                                             FAULT_GEMV_FULL))) {
                 *abort_flag = 1;
                 break;
             }
             int j, off, len;
             tc_slice(w, t, j, off, len);
-            for (int ib = 0; ib < len / TC_KB; ib++, i++) {
-                const int slot = i % D, use = i / D;
-                if (use > 0 &&
-                    !__all_sync(0xffffffffu, mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault, FAULT_GEMV_EMPTY))) {
+            for (int ib = 0; ib < len / TC_KB; ib++, i++, use += ++slot == D, slot = slot == D ? 0 : slot) {
+                if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(&aempty[slot], (use - 1) & 1, p.g.fault,
+                                                                        FAULT_GEMV_EMPTY))) {
                     *abort_flag = 1;
                     dq_ok = false;
                     break;
                 }
                 // task = (row r, 32-value half hf): 128 rows x 2 halves a sub-tile, one per thread
                 static_assert(TC_M * 2 == TC_DQT, "one 32-value task per dequantising thread");
+                if (p.ts) {
+                    // warp w writes tensor-memory lanes 32 * (w % 4) ..: row = that lane,
+                    // warps 3-6 the first 32 values of the k-block, warps 7-10 the second
+                    const int quarter = warp & 3, r = 32 * quarter + lane, hf = (warp - 3) >> 2;
+                    for (int sb = 0; sb < MS; sb++) {
+                        uint32_t h[16];
+                        tc_dequant32<DT>(Q + ((size_t)stg * MS + sb) * QB, r, ib * TC_KB + 32 * hf, h);
+                        tc_st16(tmem + ((uint32_t)(32 * quarter) << 16) + p.a_col +
+                                    (uint32_t)((slot * MS + sb) * 32 + 16 * hf),
+                                h);
+                    }
+                    tc_wait_st();
+                    tc_fence_before();   // the tensor core reads the tile after the barrier
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&afull[slot]);
+                    continue;
+                }
                 for (int sb = 0; sb < MS; sb++) {
                     const uint8_t *q = Q + ((size_t)stg * MS + sb) * QB;
                     uint8_t *tile = A + ((size_t)slot * MS + sb) * TC_M * 128;
@@ -588,7 +650,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2) k_tc_gemm(const __grid_constant
             for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                 float v[16];
                 tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(sb * npad + c0), v);
-                if (p.ksplit == 1) {
+                if (p.ksplit == 1 && p.epi == EPI_SWIGLU) {
+                    // rows (2j, 2j + 1) are (gate, up) of output j, held by a lane
+                    // pair: the even lane finishes the even columns, the odd lane
+                    // the odd ones (each lane sends the partner the value it lacks)
+                    const bool odd = lane & 1;
+                    const int pr = row & ~1;
+#pragma unroll
+                    for (int e = 0; e < 16; e += 2) {
+                        const float got = __shfl_xor_sync(0xffffffffu, odd ? v[e] : v[e + 1], 1);
+                        const int col = c0 + e + (odd ? 1 : 0);
+                        if (pr + 1 < p.g.w.rows && col < p.ncol)
+                            epi_swiglu_pair(p.g, pr, col, odd ? got : v[e], odd ? v[e + 1] : got);
+                    }
+                } else if (p.ksplit == 1) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
                         const float partner = __shfl_xor_sync(0xffffffffu, v[e], 1);
@@ -668,10 +743,13 @@ static int tc_knob(const char *name, int dflt) {
 // SM.  Spare room deepens, in this order: the activation ring (its tiles
 // are small at narrow batches, and a shallow one puts an L2 round trip
 // behind every k-block's MMA), the dequantised ring, the quantised ring.
-static void tc_rings(int dt, int npad, int ms, int &depth, int &bdepth, int &qdepth, size_t &smem, int &per_sm) {
+// With `ts` the dequantised ring lives in tensor memory (no shared memory;
+// its depth is set by the caller).
+static void tc_rings(int dt, int npad, int ms, bool ts, int &depth, int &bdepth, int &qdepth, size_t &smem,
+                     int &per_sm) {
     static const int max_per_sm = tc_knob("CMOLCU_TC_PER_SM", 2) == 1 ? 1 : 2;
     const size_t qb = (size_t)ms * tc_stage_bytes(dt), bars = (1 + 2 * TC_MAX_QD + 4 * TC_MAX_DEPTH) * 8;
-    const size_t a_slot = (size_t)ms * TC_M * 128, b_slot = (size_t)npad * 128;
+    const size_t a_slot = ts ? 0 : (size_t)ms * TC_M * 128, b_slot = (size_t)npad * 128;
     auto need = [&](int da, int db, int dq) { return 1024 + da * a_slot + db * b_slot + dq * qb + bars; };
     // CMOLCU_TC_RINGS="A,B,Q": ring depths for steps of more than 64 columns
     // (measurements), used when they fit one CTA per SM
@@ -683,7 +761,7 @@ static void tc_rings(int dt, int npad, int ms, int &depth, int &bdepth, int &qde
         smem = need(fa, fb, fq);
         return;
     }
-    for (per_sm = max_per_sm; per_sm >= 1; per_sm--) {
+    for (per_sm = ts ? 1 : max_per_sm; per_sm >= 1; per_sm--) {   // tensor-memory tiles need the whole TMEM
         const size_t budget = per_sm == 2 ? 112 * 1024 : 220 * 1024;
         depth = bdepth = qdepth = 2;
         if (need(2, 2, 2) > budget && per_sm == 2) continue;
@@ -861,16 +939,31 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     // tile, halving its shared-memory ingest per output row) for wide steps
     // on matrices with rows for well over half a wave of such CTAs, when the
     // rings still fit (not Q8_0, whose slices are twice as large).
+    // CMOLCU_TC_TS=1: the dequantised tiles go to tensor memory beside the
+    // accumulators when a ring of at least TC_TS_MIN_DEPTH of them fits in the
+    // 512 columns (one CTA an SM) at steps wider than 128 columns, so the
+    // tensor core reads only the activation tiles from shared memory (one
+    // 128-row sub-tile then).  Off by default: measured on the config-4
+    // shapes at 256 columns it ties the shared-memory form on the split-K
+    // matrices and loses on the 22016-row one, whose two-sub-tile CTAs it
+    // cannot hold (2 x 256 accumulator columns fill the tensor memory).
     static const int ms_knob = tc_knob("CMOLCU_TC_MSUB", 0);
+    static const bool ts_on = tc_knob("CMOLCU_TC_TS", 0) != 0;
     int ms = (npad >= 128 && w.rows >= 2 * TC_M * 64 && w.dtype != DT_Q8_0) ? 2 : 1;
+    if (ts_on && npad > 128) ms = 1;
     if (ms_knob == 1 || ms_knob == 2) ms = ms_knob;
     int depth, bdepth, qdepth, per_sm;
     size_t smem;
-    tc_rings(w.dtype, npad, ms, depth, bdepth, qdepth, smem, per_sm);
+    auto ts_acol = [&](int m) { return (m * npad + 31) / 32 * 32; };   // the ring starts on a 32-column boundary
+    auto ts_depth = [&](int m) { return std::min(TC_TS_MAX_DEPTH, (512 - ts_acol(m)) / (m * 32)); };
+    bool ts = ts_on && npad > 128 && ts_depth(ms) >= TC_TS_MIN_DEPTH;
+    tc_rings(w.dtype, npad, ms, ts, depth, bdepth, qdepth, smem, per_sm);
     if (ms == 2 && smem > 220 * 1024) {
         ms = 1;
-        tc_rings(w.dtype, npad, ms, depth, bdepth, qdepth, smem, per_sm);
+        ts = ts_on && npad > 128 && ts_depth(ms) >= TC_TS_MIN_DEPTH;
+        tc_rings(w.dtype, npad, ms, ts, depth, bdepth, qdepth, smem, per_sm);
     }
+    if (ts) depth = ts_depth(ms);
     const int nslice = tc_nslice(w.k, w.kc);
     int rb, ks, sps;
     tc_split(w.rows, nslice, per_sm, ms, rb, ks, sps);
@@ -889,7 +982,9 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     p.part = s.part;
     p.counters = s.counters;
     p.msub = ms;
-    const int tcols = ms * npad;
+    p.ts = ts ? 1 : 0;
+    p.a_col = (uint32_t)ts_acol(ms);
+    const int tcols = ts ? ts_acol(ms) + depth * ms * 32 : ms * npad;
     p.tmem_cols = tcols <= 32 ? 32 : tcols <= 64 ? 64 : tcols <= 128 ? 128 : tcols <= 256 ? 256 : 512;
     p.depth = depth;
     p.bdepth = bdepth;
@@ -915,7 +1010,7 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     if (smem > attr_done[dev][di]) return cudaErrorInvalidConfiguration;
     // split partials through distributed shared memory when the splits fit in
     // one cluster and a partial ([npad][128] floats) fits in the drained rings
-    const size_t rings = (size_t)depth * ms * TC_M * 128 + (size_t)bdepth * npad * 128 +
+    const size_t rings = (ts ? (size_t)0 : (size_t)depth * ms * TC_M * 128) + (size_t)bdepth * npad * 128 +
                          (size_t)qdepth * ms * tc_stage_bytes(w.dtype);
     static const bool no_cluster = tc_knob("CMOLCU_TC_CLUSTER", 1) == 0;
     p.cluster = !no_cluster && ks > 1 && (size_t)npad * TC_M * 4 <= rings && tc_cluster_ok(k, ks, rb, smem) ? 1 : 0;

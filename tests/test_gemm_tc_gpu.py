@@ -22,11 +22,17 @@ CASES = [
     (synth.Q5_0, 512, 2048, 64),
     (synth.Q8_0, 19200, 512, 16),     # > 148 row blocks: no K split, epilogue from tensor memory
     (synth.Q4_K, 1024, 4096, 256),    # the widest column count
-    # >= 64 blocks of 256 rows at 128+ columns: two 128-row sub-tiles per CTA
+    # >= 64 blocks of 256 rows at 128 columns: two 128-row sub-tiles per CTA
     # (two tensor-memory accumulators share each activation tile); the last
     # block is ragged (a partial second sub-tile)
     (synth.Q4_K, 16512, 512, 256),
+    (synth.Q4_0, 16448, 256, 128),
+    # wider than 128 columns: every format, ragged widths, split K through a
+    # cluster (also run with the dequantised tiles in tensor memory below)
     (synth.Q4_0, 16448, 256, 130),
+    (synth.Q8_0, 300, 1024, 200),
+    (synth.Q5_0, 2048, 1024, 256),
+    (synth.Q4_K, 512, 8192, 256),
 ]
 
 
@@ -104,4 +110,30 @@ print("ok")
 """
     env = dict(os.environ, CMOLCU_TC_CLUSTER="0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_batched_tensor_memory_tiles(gpu):
+    """With CMOLCU_TC_TS=1 (read once per process) steps wider than 128
+    columns keep the dequantised tiles in tensor memory and the tensor core
+    reads A from there; the cases wider than 128 columns, same bound, in a
+    fresh process."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = f"""
+import sys
+sys.path.insert(0, {os.path.dirname(here)!r})
+sys.path.insert(0, {here!r})
+import torch
+import test_gemm_tc_gpu as t
+dev = torch.device("cuda:0")
+for case in [c for c in t.CASES if c[3] > 128]:
+    t.test_batched_matches_exact(dev, *case, norm=True)
+print("ok")
+"""
+    env = dict(os.environ, CMOLCU_TC_TS="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
