@@ -788,8 +788,16 @@ static int tc_nslice(int k, int kc) {
     return (nkc - 1) * (kc / TC_SV) + (last + TC_SV - 1) / TC_SV;
 }
 
-static void tc_split(int rows, int nslice, int per_sm, int ms, int &rblocks, int &ksplit, int &sps) {
-    static const int cap = std::max(1, tc_knob("CMOLCU_TC_KSPLIT_MAX", 1 << 20));
+// K split of a row block: as many splits as fill one wave of CTAs, at most
+// `wide_cap` of them at steps wider than 128 columns.  There each split's
+// partial is npad x 128 floats and the reduction's cost grows with the number
+// of splits faster than the extra SMs pay back: at 256 columns, capping the
+// split at 6 took 2048 x 11008 from 60.3 to 43.6 us and 2048 x 2048 from 28.6
+// to 18.9 us (graph replay); caps 2, 3 and 4 measured slower than 6.
+#define TC_WIDE_KSPLIT 6
+static void tc_split(int rows, int nslice, int per_sm, int ms, int npad, int &rblocks, int &ksplit, int &sps) {
+    static const int knob = tc_knob("CMOLCU_TC_KSPLIT_MAX", 0);
+    const int cap = knob > 0 ? knob : npad > 128 ? TC_WIDE_KSPLIT : 1 << 20;
     const int slots = device_sm_count() * per_sm;
     rblocks = (rows + TC_M * ms - 1) / (TC_M * ms);
     ksplit = ms > 1 ? 1 : std::max(1, std::min(std::min(nslice, cap), slots / rblocks));    // one wave
@@ -801,7 +809,7 @@ void tc_scratch_need(int rows, int k, int ncol, size_t *xs_halves, size_t *part_
     const int npad = tc_npad(ncol);
     *xs_halves = (size_t)k * npad;
     int rb, ks, sps;
-    tc_split(rows, k / TC_KB, 2, 1, rb, ks, sps);     // an upper bound on the split of any format
+    tc_split(rows, k / TC_KB, 2, 1, 16, rb, ks, sps);   // an upper bound on the split of any format and width
     *part_floats = ks > 1 ? (size_t)rb * ks * npad * TC_M : 0;
     *row_blocks = rb;
 }
@@ -966,7 +974,7 @@ cudaError_t tc_matmul(const GemvArgs &a, int ncol, int epi, const TcScratch &s, 
     if (ts) depth = ts_depth(ms);
     const int nslice = tc_nslice(w.k, w.kc);
     int rb, ks, sps;
-    tc_split(w.rows, nslice, per_sm, ms, rb, ks, sps);
+    tc_split(w.rows, nslice, per_sm, ms, npad, rb, ks, sps);
     if (!s.xs || rb > s.max_row_blocks || (ks > 1 && (size_t)rb * ks * npad * TC_M > s.part_floats))
         return cudaErrorInvalidValue;
     TcParams p = {};
