@@ -125,14 +125,30 @@ __global__ void __launch_bounds__(256) k_tc_xprep(const float *x, long long x_ld
         __syncthreads();
         ir = s_ir;
     }
+    // 8 consecutive values a thread per pass: two 16-byte loads of x (and of
+    // the gains) when the column's start is 16-byte aligned
+    const bool vec = live && ((reinterpret_cast<uintptr_t>(xc) | reinterpret_cast<uintptr_t>(norm_w)) & 15) == 0;
     for (int c = tid; c < K / 8; c += 256) {
         const int k0 = c * 8, kb = k0 >> 6, ch = (k0 & 63) >> 3;
         float v[8];
+        if (vec) {
+            const float4 a = *reinterpret_cast<const float4 *>(xc + k0);
+            const float4 b = *reinterpret_cast<const float4 *>(xc + k0 + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            if (norm_w) {
+                const float4 ga = *reinterpret_cast<const float4 *>(norm_w + k0);
+                const float4 gb = *reinterpret_cast<const float4 *>(norm_w + k0 + 4);
+                const float g[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float t = live ? xc[k0 + i] : 0.f;
-            if (live && norm_w) t = __fmul_rn(norm_w[k0 + i], __fmul_rn(t, ir));
-            v[i] = t;
+                for (int i = 0; i < 8; i++) v[i] = __fmul_rn(g[i], __fmul_rn(v[i], ir));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                float t = live ? xc[k0 + i] : 0.f;
+                if (live && norm_w) t = __fmul_rn(norm_w[k0 + i], __fmul_rn(t, ir));
+                v[i] = t;
+            }
         }
         uint4 o = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
         uint4 *dst = reinterpret_cast<uint4 *>(xs + ((size_t)kb * npad + n) * 64) + (ch ^ (n & 7));
@@ -789,15 +805,17 @@ static int tc_nslice(int k, int kc) {
 }
 
 // K split of a row block: as many splits as fill one wave of CTAs, at most
-// `wide_cap` of them at steps wider than 128 columns.  There each split's
+// TC_WIDE_KSPLIT of them at steps of 128 columns or more.  There each split's
 // partial is npad x 128 floats and the reduction's cost grows with the number
 // of splits faster than the extra SMs pay back: at 256 columns, capping the
 // split at 6 took 2048 x 11008 from 60.3 to 43.6 us and 2048 x 2048 from 28.6
-// to 18.9 us (graph replay); caps 2, 3 and 4 measured slower than 6.
+// to 18.9 us (graph replay; caps 2, 3 and 4 measured slower than 6); at 128
+// columns 2048 x 11008 from 44.2 to 37.3 us.  At 32 and 64 columns the cap
+// measured no better.
 #define TC_WIDE_KSPLIT 6
 static void tc_split(int rows, int nslice, int per_sm, int ms, int npad, int &rblocks, int &ksplit, int &sps) {
     static const int knob = tc_knob("CMOLCU_TC_KSPLIT_MAX", 0);
-    const int cap = knob > 0 ? knob : npad > 128 ? TC_WIDE_KSPLIT : 1 << 20;
+    const int cap = knob > 0 ? knob : npad >= 128 ? TC_WIDE_KSPLIT : 1 << 20;
     const int slots = device_sm_count() * per_sm;
     rblocks = (rows + TC_M * ms - 1) / (TC_M * ms);
     ksplit = ms > 1 ? 1 : std::max(1, std::min(std::min(nslice, cap), slots / rblocks));    // one wave
