@@ -161,7 +161,7 @@ def run_batched(args, rank, world, local, barrier, dist=None):
                    "prompt_scale": args.prompt_scale,
                    "note": "prompts run through the decode step one token per session per step"},
         "e2e": {"value": round(gen_all / (wall_ms / 1e3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": 4 * (4 * sessions + 1 + 3 * sessions), "d2h_bytes_per_step": 4 * (sessions + 1)},
+                "h2d_bytes_per_step": int(st.h2d_bytes_per_step), "d2h_bytes_per_step": int(st.d2h_bytes_per_step)},
         "prefill_tokens_per_s": round(prefill_all / (dev_ms / 1e3), 1),
         "gpu_launches": int(steps * launches),
         "clocks": clocks.summary(),
@@ -284,7 +284,7 @@ def run_decode_aggregate(args, rank, world, local, barrier, dist=None):
                    "decode_steps_timed": int(steps_max),
                    "l2": "each step reads every weight and every session's KV (GBs), far above the 126 MB L2"},
         "e2e": {"value": round(tok_all / (wall_ms / 1e3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": 4 * (7 * sessions + 1), "d2h_bytes_per_step": 4 * (sessions + 1)},
+                "h2d_bytes_per_step": int(st.h2d_bytes_per_step), "d2h_bytes_per_step": int(st.d2h_bytes_per_step)},
         "roofline": roof,
         "kernels": kernels,
         "cpu_baseline": cpu,
@@ -797,8 +797,8 @@ def run_single(args, rank, world, local, barrier, dist, workload, steps=None, wi
                        "weights_bytes_per_step": sweep_bytes,
                        "l2": "weights streamed per step exceed the 126 MB L2 (no flush needed)"
                              if sweep_bytes > 126e6 else "weights fit in L2: steady state, not flushed"},
-            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * (4 * 1 + 1 + 3),
-                    "d2h_bytes_per_step": 4 * 2},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(st.h2d_bytes_per_step),
+                    "d2h_bytes_per_step": int(st.d2h_bytes_per_step)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "k_gemv (all GEMV launches of one decode step, graph replay)",

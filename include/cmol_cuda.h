@@ -117,7 +117,12 @@ typedef struct {
                                     pipeline wait, 3 token id outside the
                                     vocabulary, 4 page outside the pool,
                                     5 sampler found no finite candidate,
-                                    6 attention page wait               */
+                                    6 attention page wait, 7 planted
+                                    wait (cmol_cuda_debug_inject 3)     */
+    long long h2d_bytes_per_step;   /* host -> device bytes one step copies
+                                       (its metadata)                    */
+    long long d2h_bytes_per_step;   /* device -> host bytes one step copies
+                                       (sampled ids and the fault word)  */
 } cmol_cuda_stats_t;
 
 cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int gpu_index, cmol_cuda_stats_t *out);
@@ -151,7 +156,10 @@ cmol_err_t cmol_cuda_kernel_sweep(cmol_model_t *m, int gpu_index, int what, int 
  * planted error that the kernels' own bounds checks catch, record in the
  * device fault word and skip (no out-of-range access happens):
  *   kind 1: column 0's token id is vocab + 3 (code 3);
- *   kind 2: a page-table update names a page past the pool (code 4).
+ *   kind 2: a page-table update names a page past the pool (code 4);
+ *   kind 3: the step's first kernel waits on a barrier that nothing arrives
+ *           on until its bounded wait runs out (a few ms; code 7), as any
+ *           device wait does when an arrival is lost.
  * That step fails: the requests in it return CMOL_ERR_INVALID, and
  * cmol_cuda_stats reports the code.  Later steps run normally. */
 cmol_err_t cmol_cuda_debug_inject(cmol_model_t *m, int gpu_index, int kind);

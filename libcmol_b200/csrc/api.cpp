@@ -893,6 +893,8 @@ extern "C" cmol_err_t cmol_cuda_stats(const cmol_model_t *m, int g, cmol_cuda_st
     out->steps = e->stats.steps;
     out->step_ms_total = e->stats.step_ms_total;
     out->last_fault_code = e->last_fault();
+    out->h2d_bytes_per_step = e->h2d_bytes_per_step();
+    out->d2h_bytes_per_step = e->d2h_bytes_per_step();
     return CMOL_OK;
 }
 
@@ -913,7 +915,7 @@ extern "C" cmol_err_t cmol_cuda_kernel_sweep(cmol_model_t *m, int g, int what, i
 }
 
 extern "C" cmol_err_t cmol_cuda_debug_inject(cmol_model_t *m, int g, int kind) {
-    if (!m || g < 0 || g >= (int)m->workers.size() || kind < 1 || kind > 2) return CMOL_ERR_ARGS;
+    if (!m || g < 0 || g >= (int)m->workers.size() || kind < 1 || kind > 3) return CMOL_ERR_ARGS;
     m->workers[(size_t)g]->eng->inject_fault(kind);
     return CMOL_OK;
 }

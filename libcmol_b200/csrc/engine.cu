@@ -315,7 +315,7 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     d->counters = b.dalloc<int>((size_t)B * nkv);
 
     d->slots = b.dalloc<SlotSampler>((size_t)o.max_slots);
-    d->meta_ints = (size_t)4 * B + 1 + 3 * (size_t)B + B + (B + 1) + 2;
+    d->meta_ints = (size_t)4 * B + 1 + 3 * (size_t)B + B + (B + 1) + 3;
     d->meta_dev = b.dalloc<int>(d->meta_ints);
     d->out_dev = b.dalloc<int>((size_t)B + 1);   // + the fault word, read back with the ids
     d->fault = reinterpret_cast<unsigned int *>(d->out_dev + B);
@@ -337,6 +337,7 @@ Engine *Engine::create(int device, const HostModel &m, const EngineOptions &o, i
     d->meta.chunk_pfx = d->meta_dev + 8 * B + 1;
     d->meta.attn_n = d->meta_dev + 9 * B + 2;
     d->meta.attn_chunk = d->meta_dev + 9 * B + 3;
+    d->meta.stall = d->meta_dev + 9 * B + 4;
     d->work = b.dalloc<int>((size_t)2 * L);
     if (!d->work) return fail(-1);
 
@@ -607,6 +608,8 @@ static cudaError_t record_step(Engine::Impl *d, const EngineOptions &o, int ncol
 // chunk size, the largest power-of-two multiple of 64 tokens (up to 4096)
 // that still gives about six (chunk, kv head) items per SM; and the prefix
 // sums of the columns' chunk counts.
+long long Engine::h2d_bytes_per_step() const { return d ? (long long)d->meta_ints * 4 : 0; }
+
 static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, int n_kv, int page_tokens) {
     int *order = m + 7 * B + 1, *pfx = m + 8 * B + 1;
     int nl = 0;
@@ -665,10 +668,12 @@ int Engine::step(const std::vector<StepColumn> &cols, const std::vector<PageUpda
         m[4 * B + 2 + 3 * u] = upd[u].index;
         m[4 * B + 3 + 3 * u] = upd[u].page;
     }
-    // planted errors of the fault-path tests: both are caught by the bounds
-    // checks of k_step_begin, which record the code and skip the access
+    // planted errors of the fault-path tests: kinds 1 and 2 are caught by the
+    // bounds checks of k_step_begin, which record the code and skip the
+    // access; kind 3 makes k_step_begin's bounded wait run out (code 7)
     attention_plan(m, cols, B, d->hp.n_kv_heads, opt_.page_tokens);
     const int inject = inject_.exchange(0);
+    m[9 * B + 4] = inject == 3 ? 1 : 0;
     if (inject == 1) {
         m[0] = vocab_ + 3;
     } else if (inject == 2 && (int)upd.size() < B) {

@@ -104,8 +104,13 @@ class Engine {
     const char *last_error() const { return err_; }
     // Fault-path test hook: the next step carries a planted error that the
     // device checks catch and skip (1: column 0's token id past the
-    // vocabulary; 2: a page-table update naming a page outside the pool).
+    // vocabulary; 2: a page-table update naming a page outside the pool;
+    // 3: the step-begin kernel's bounded wait runs out).
     void inject_fault(int kind) { inject_.store(kind); }
+    // Bytes one step copies host -> device (its metadata) and device -> host
+    // (sampled ids and the fault word), logits excluded.
+    long long h2d_bytes_per_step() const;
+    long long d2h_bytes_per_step() const { return 4LL * (opt_.max_batch + 1); }
     // Device fault code of the last failed step (0 = none since load).
     unsigned int last_fault() const { return last_fault_; }
     EngineStats stats;

@@ -60,6 +60,25 @@ __global__ void k_step_begin(StepBeginArgs a) {
     pdl_wait();
     pdl_launch_dependents();
     const int col = blockIdx.x;
+    if (col == 0 && threadIdx.x == 0 && *a.meta.stall) {
+        // fault-path test: a wait on a barrier that nothing arrives on, bounded
+        // by polling (mbarrier.test_wait never suspends: ~2^20 polls, a few ms),
+        // records its code like every other wait that runs out
+        __shared__ uint64_t never;
+        mbar_init(&never, 1);
+        fence_mbar_init();
+        bool done = false;
+        for (uint32_t i = 0; i < (1u << 20) && !done; i++) {
+            uint32_t ok;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], 0;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(ok)
+                : "r"(smem_u32(&never))
+                : "memory");
+            done = ok != 0;
+        }
+        if (!done && a.fault) atomicExch(a.fault, FAULT_STEP_WAIT);
+    }
     if (col == 0) {
         const int n = *a.meta.n_upd;
         for (int u = threadIdx.x; u < n; u += blockDim.x) {

@@ -32,6 +32,7 @@ struct StepMetaPtrs {
     int *chunk_pfx;  // [B+1] prefix sums of their attention chunk counts
     int *attn_n;     // [1] live columns
     int *attn_chunk; // [1] context tokens per attention work item
+    int *stall;      // [1] 1: k_step_begin waits on a barrier nothing arrives on (fault-path test)
 };
 
 struct StepBeginArgs {

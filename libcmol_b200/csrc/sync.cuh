@@ -18,6 +18,7 @@ enum : unsigned int {
     FAULT_BAD_PAGE = 4,        // a page-table update outside the table / pool
     FAULT_SAMPLE = 5,          // the sampler found no valid candidate (non-finite logits)
     FAULT_ATTN_WAIT = 6,       // attention waited too long for its K/V pages
+    FAULT_STEP_WAIT = 7,       // the step-begin kernel's wait ran out (cmol_cuda_debug_inject kind 3)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

@@ -59,7 +59,8 @@ class CudaStats(C.Structure):
                 ("step_ms_last", C.c_double), ("weight_bytes", C.c_longlong),
                 ("kv_bytes_read", C.c_longlong), ("kernel_launches_per_step", C.c_int),
                 ("graph_steps", C.c_int), ("steps", C.c_longlong), ("step_ms_total", C.c_double),
-                ("last_fault_code", C.c_uint)]
+                ("last_fault_code", C.c_uint), ("h2d_bytes_per_step", C.c_longlong),
+                ("d2h_bytes_per_step", C.c_longlong)]
 
 
 class BatchItem(C.Structure):

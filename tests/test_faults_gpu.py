@@ -2,8 +2,10 @@
 
 cmol_cuda_debug_inject plants an error in the next decode step that the
 kernels' own bounds checks catch: a token id past the vocabulary (the
-embedding read is skipped, code 3) or a page-table update naming a page
-outside the pool (the table write is skipped, code 4).  The step must fail
+embedding read is skipped, code 3), a page-table update naming a page
+outside the pool (the table write is skipped, code 4), or a wait on a
+barrier that nothing arrives on, which runs out after its bound (code 7):
+the path every lost arrival takes.  The step must fail
 with CMOL_ERR_INVALID carrying the code (the reference's generate loop
 returns CMOL_ERR_INVALID when a forward fails, src/api.c:454,520), and the
 next request on the same session pool must be served correctly.
@@ -27,7 +29,7 @@ def tiny(tmp_path_factory):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("kind,code", [(1, 3), (2, 4)], ids=["bad_token", "bad_page"])
+@pytest.mark.parametrize("kind,code", [(1, 3), (2, 4), (3, 7)], ids=["bad_token", "bad_page", "wait_runs_out"])
 def test_planted_fault_fails_step_then_recovers(gpu, tiny, kind, code):
     from libcmol_b200.model import GenParams, Model
     g = np.load(os.path.join(GOLD, "models.npz"))
