@@ -93,6 +93,23 @@ cmol_err_t cmol_forward_logits_batch(cmol_session_t *const *ss, const int32_t *t
 
 int cmol_session_n_tokens(const cmol_session_t *s);
 int cmol_session_device(const cmol_session_t *s);
+
+/* Session KV snapshots for multi-turn reuse (call between requests, with no
+ * request of the session in flight).
+ *   cmol_cuda_session_save: writes the session's context (its token count and
+ *     the K and V of every cached position, all layers, in the engine's KV
+ *     format) to buf and its size to *size; with buf NULL only the size.
+ *     CMOL_ERR_TRUNC when cap is smaller than the size.
+ *   cmol_cuda_session_restore: loads a snapshot into a session of a model
+ *     with the same layer count, vocabulary, KV format and page size (on any
+ *     of its GPUs): the session continues from that context, as if it had
+ *     run those tokens.  CMOL_ERR_INVALID for a snapshot of another shape,
+ *     CMOL_ERR_CTX_FULL past the model's context, CMOL_ERR_OOM when its GPU
+ *     has no free KV pages left.  The weights are not compared: restoring a
+ *     snapshot taken with another model of the same shapes gives that
+ *     model's context. */
+cmol_err_t cmol_cuda_session_save(cmol_session_t *s, void *buf, size_t cap, size_t *size);
+cmol_err_t cmol_cuda_session_restore(cmol_session_t *s, const void *buf, size_t size);
 int cmol_vocab_size(const cmol_model_t *m);
 int cmol_eos_id(const cmol_model_t *m);
 

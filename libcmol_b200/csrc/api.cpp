@@ -381,6 +381,78 @@ extern "C" void cmol_session_reset(cmol_session_t *s) {
     s->n_tokens = 0;   // pages stay with the session for its next turn
 }
 
+// ---------------------------------------------------------------------------
+// Session KV snapshots: a header and the K / V of every page the session's
+// context occupies, all layers, in the engine's KV format.
+// ---------------------------------------------------------------------------
+namespace {
+struct KvSnapshotHeader {
+    uint32_t magic, version;
+    int32_t  n_layers, page_tokens, kv_f16, vocab;
+    int64_t  page_bytes;                 // one page of one layer
+    int32_t  n_tokens, n_pages;
+};
+const uint32_t kSnapMagic = 0x564B4D43u;   // "CMKV"
+}  // namespace
+
+extern "C" cmol_err_t cmol_cuda_session_save(cmol_session_t *s, void *buf, size_t cap, size_t *size) {
+    if (!s || !size) return CMOL_ERR_ARGS;
+    Engine *e = s->model->workers[(size_t)s->gpu]->eng.get();
+    const int P = e->page_tokens();
+    KvSnapshotHeader h = {};
+    h.magic = kSnapMagic;
+    h.version = 1;
+    h.n_layers = e->n_layers();
+    h.page_tokens = P;
+    h.kv_f16 = e->kv_f16() ? 1 : 0;
+    h.vocab = s->model->vocab;
+    h.page_bytes = e->kv_page_bytes();
+    h.n_tokens = s->n_tokens;
+    h.n_pages = (s->n_tokens + P - 1) / P;
+    const size_t need = sizeof h + (size_t)h.n_layers * h.n_pages * (size_t)h.page_bytes;
+    *size = need;
+    if (!buf) return CMOL_OK;
+    if (cap < need) return CMOL_ERR_TRUNC;
+    if (h.n_pages > (int)s->pages.size()) return CMOL_ERR_INVALID;
+    memcpy(buf, &h, sizeof h);
+    if (e->kv_pages_copy(s->pages.data(), h.n_pages, static_cast<unsigned char *>(buf) + sizeof h, true) != 0)
+        return CMOL_ERR_INVALID;
+    return CMOL_OK;
+}
+
+extern "C" cmol_err_t cmol_cuda_session_restore(cmol_session_t *s, const void *buf, size_t size) {
+    if (!s || !buf || size < sizeof(KvSnapshotHeader)) return CMOL_ERR_ARGS;
+    KvSnapshotHeader h;
+    memcpy(&h, buf, sizeof h);
+    Worker *w = s->model->workers[(size_t)s->gpu].get();
+    Engine *e = w->eng.get();
+    const int P = e->page_tokens();
+    if (h.magic != kSnapMagic || h.version != 1 || h.n_layers != e->n_layers() || h.page_tokens != P ||
+        h.kv_f16 != (e->kv_f16() ? 1 : 0) || h.vocab != s->model->vocab || h.page_bytes != e->kv_page_bytes() ||
+        h.n_tokens < 0 || h.n_pages != (h.n_tokens + P - 1) / P)
+        return CMOL_ERR_INVALID;
+    if (h.n_tokens > e->max_ctx()) return CMOL_ERR_CTX_FULL;
+    if (size != sizeof h + (size_t)h.n_layers * h.n_pages * (size_t)h.page_bytes) return CMOL_ERR_ARGS;
+    {
+        // the session's own pages first, then pages from its GPU's free list
+        std::lock_guard<std::mutex> lk(w->mu);
+        const size_t want = (size_t)h.n_pages;
+        if (s->pages.size() < want && w->free_pages.size() < want - s->pages.size()) return CMOL_ERR_OOM;
+        while (s->pages.size() < want) {
+            s->pages.push_back(w->free_pages.back());
+            w->free_pages.pop_back();
+        }
+    }
+    if (e->kv_pages_copy(s->pages.data(), h.n_pages, const_cast<unsigned char *>(
+                                                          static_cast<const unsigned char *>(buf) + sizeof h),
+                         false) != 0 ||
+        e->set_page_row(s->lslot, s->pages.data(), (int)s->pages.size()) != 0)
+        return CMOL_ERR_INVALID;
+    w->load += h.n_tokens - s->n_tokens;
+    s->n_tokens = h.n_tokens;
+    return CMOL_OK;
+}
+
 extern "C" int cmol_session_n_tokens(const cmol_session_t *s) { return s ? s->n_tokens : 0; }
 extern "C" int cmol_session_device(const cmol_session_t *s) { return s ? s->gpu : -1; }
 extern "C" int cmol_vocab_size(const cmol_model_t *m) { return m ? m->vocab : 0; }

@@ -453,6 +453,48 @@ static void *kv_layer(const Engine::Impl *d, int l, const EngineOptions &o) {
     return static_cast<unsigned char *>(d->kv_pages) + (size_t)l * d->n_pages * d->page_elems * (o.kv_f16 ? 2 : 4);
 }
 
+long long Engine::kv_page_bytes() const { return d ? d->page_elems * (opt_.kv_f16 ? 2 : 4) : 0; }
+int Engine::n_layers() const { return d ? d->hp.n_layers : 0; }
+
+int Engine::kv_pages_copy(const int *pages, int n, void *host, bool to_host) {
+    if (!d || n < 0 || (n > 0 && (!pages || !host))) return -1;
+    cudaSetDevice(device_);
+    const size_t pb = (size_t)kv_page_bytes();
+    unsigned char *h = static_cast<unsigned char *>(host);
+    for (int i = 0; i < n; i++)
+        if (pages[i] < 0 || pages[i] >= n_pages_) {
+            snprintf(err_, sizeof err_, "kv copy: page %d outside the pool", pages[i]);
+            return -1;
+        }
+    for (int l = 0; l < d->hp.n_layers; l++) {
+        unsigned char *base = static_cast<unsigned char *>(kv_layer(d, l, opt_));
+        for (int i = 0; i < n; i++) {
+            unsigned char *dv = base + (size_t)pages[i] * pb;
+            unsigned char *hv = h + ((size_t)l * n + i) * pb;
+            const cudaError_t e = to_host ? cudaMemcpy(hv, dv, pb, cudaMemcpyDeviceToHost)
+                                          : cudaMemcpy(dv, hv, pb, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                snprintf(err_, sizeof err_, "kv copy: %s", cudaGetErrorString(e));
+                return -1;
+            }
+        }
+    }
+    return 0;
+}
+
+int Engine::set_page_row(int lslot, const int *pages, int n) {
+    if (!d || lslot < 0 || lslot >= opt_.max_slots || n < 0 || n > max_pages_ || (n > 0 && !pages)) return -1;
+    if (n == 0) return 0;
+    cudaSetDevice(device_);
+    const cudaError_t e =
+        cudaMemcpy(d->page_table + (size_t)lslot * max_pages_, pages, (size_t)n * sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        snprintf(err_, sizeof err_, "page table: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
 // What record_step records: the whole step, only its weight products, or
 // only its attention launches (the last two for the kernel sweeps).
 enum { REC_FULL = 0, REC_MATMUL = 1, REC_ATTN = 2 };

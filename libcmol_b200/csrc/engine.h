@@ -107,6 +107,17 @@ class Engine {
     // vocabulary; 2: a page-table update naming a page outside the pool;
     // 3: the step-begin kernel's bounded wait runs out).
     void inject_fault(int kind) { inject_.store(kind); }
+    // Session KV snapshots (multi-turn reuse).  kv_pages_copy moves pages
+    // pages[0..n) of every layer to host memory laid out [layer][page][page
+    // bytes] (to_host) or back into those pages; set_page_row writes engine
+    // slot lslot's page-table entries [0, n).  Both synchronous, on no engine
+    // stream: the caller keeps the session idle meanwhile.
+    int kv_pages_copy(const int *pages, int n, void *host, bool to_host);
+    int set_page_row(int lslot, const int *pages, int n);
+    long long kv_page_bytes() const;   // one page of one layer
+    int n_layers() const;
+    int max_ctx() const { return opt_.max_ctx; }
+    bool kv_f16() const { return opt_.kv_f16; }
     // Bytes one step copies host -> device (its metadata) and device -> host
     // (sampled ids and the fault word), logits excluded.
     long long h2d_bytes_per_step() const;

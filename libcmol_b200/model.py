@@ -107,6 +107,8 @@ def api():
                                             C.POINTER(C.c_longlong), C.POINTER(C.c_double), C.POINTER(C.c_int)])
     sig("cmol_session_n_tokens", C.c_int, [_vp])
     sig("cmol_session_device", C.c_int, [_vp])
+    sig("cmol_cuda_session_save", C.c_int, [_vp, _vp, C.c_size_t, C.POINTER(C.c_size_t)])
+    sig("cmol_cuda_session_restore", C.c_int, [_vp, _vp, C.c_size_t])
     sig("cmol_vocab_size", C.c_int, [_vp])
     sig("cmol_eos_id", C.c_int, [_vp])
     sig("cmol_cuda_stats", C.c_int, [_vp, C.c_int, C.POINTER(CudaStats)])
@@ -256,6 +258,18 @@ class Session:
     @property
     def device(self) -> int:
         return api().cmol_session_device(self.h)
+
+    def save(self) -> bytes:
+        """cmol_cuda_session_save: the session's KV snapshot."""
+        n = C.c_size_t(0)
+        _chk(api().cmol_cuda_session_save(self.h, None, 0, C.byref(n)), "cmol_cuda_session_save")
+        buf = C.create_string_buffer(n.value)
+        _chk(api().cmol_cuda_session_save(self.h, buf, n.value, C.byref(n)), "cmol_cuda_session_save")
+        return buf.raw
+
+    def restore(self, snap: bytes):
+        """cmol_cuda_session_restore: continue from a saved context."""
+        _chk(api().cmol_cuda_session_restore(self.h, snap, len(snap)), "cmol_cuda_session_restore")
 
     def forward_logits(self, token: int) -> np.ndarray:
         out = np.zeros(self.m.vocab, np.float32)
