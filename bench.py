@@ -338,19 +338,21 @@ def run_gemv_microbench(args, rank, local):
         ncopy = max(2, int(2 * 2 * 126e6 // nbytes) + 1)
         ws = [Weight(blob, dt, GEMV_M, GEMV_K) for _ in range(ncopy)]
         row = {}
-        for n in (1, 2, 4, 8, 16, 32, 64, 128):
+        has_tc = dt in (synth.Q4_K, synth.Q8_0, synth.Q4_0, synth.Q5_0)
+        # both paths where they overlap (n = 4..16: the crossover), the exact
+        # GEMV alone below, the tensor cores alone above
+        runs = [(n, False) for n in (1, 2, 4, 8, 16)] + [(n, True) for n in (4, 8, 16, 32, 64, 128) if has_tc]
+        for n, tc in runs:
             x = torch.randn(n, GEMV_K, device=f"cuda:{local}")
             y = torch.zeros(n, GEMV_M, device=f"cuda:{local}")
-            tc = n >= 4 and dt in (synth.Q4_K, synth.Q8_0, synth.Q4_0, synth.Q5_0)
-            if n > 2 and not tc:
-                continue
             fn = matmul_batched_bench if tc else gemv_bench
             fn(ws, x, y, n, iters=2 * ncopy, reps=2)                      # warm-up
             ms = fn(ws, x, y, n, iters=4 * ncopy, reps=max(3, args.steps // 16))
             gbs = nbytes / (ms * 1e-3) / 1e9
             tfs = 2.0 * GEMV_M * GEMV_K * n / (ms * 1e-3) / 1e12
-            row[str(n)] = {"path": "tcgen05" if tc else "gemv", "us": round(ms * 1e3, 3), "GBps": round(gbs, 1),
-                           "frac": round(gbs / peak, 4), "TFLOPs": round(tfs, 2)}
+            key = str(n) if (tc or n <= 2 or not has_tc) else f"{n}_gemv"
+            row[key] = {"path": "tcgen05" if tc else "gemv", "us": round(ms * 1e3, 3), "GBps": round(gbs, 1),
+                        "frac": round(gbs / peak, 4), "TFLOPs": round(tfs, 2)}
         res[synth.DTYPE_NAMES[dt]] = {"bytes": nbytes, "copies": ncopy, "n": row}
         for w in ws:
             w.free()

@@ -92,7 +92,8 @@ int cmolcu_matmul_batched_bench(cmolcu_weight_t *const *ws, int nw, const float 
                                 int iters, int reps, float *ms_per_matmul);
 
 /* Microbenchmark: `iters` back-to-back GEMVs (rotating over the nw weights,
- * all of one shape, n = 1 or 2 columns, x [n][k], y [n][rows] on the
+ * all of one shape, n = 1..16 columns (one launch per 2, as the engine runs
+ * them), x [n][k], y [n][rows] on the
  * device), captured once in a CUDA graph with programmatic dependent launch
  * and replayed `reps` times.  *ms_per_gemv is device time per GEMV measured
  * with CUDA events on the replay stream. */

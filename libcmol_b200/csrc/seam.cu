@@ -285,10 +285,11 @@ extern "C" int cmolcu_matmul_batched_bench(cmolcu_weight_t *const *ws, int nw, c
 
 // Back-to-back GEMVs over `nw` distinct weights (all the same shape), captured
 // in one CUDA graph with programmatic dependent launch between them, replayed
-// `reps` times; *ms_per_gemv = device time per GEMV (CUDA events).
+// `reps` times; *ms_per_gemv = device time per GEMV (CUDA events).  n <= 16
+// columns, launched as the engine does (one launch per 2 columns).
 extern "C" int cmolcu_gemv_bench(cmolcu_weight_t *const *ws, int nw, const float *x, int n, float *y,
                                  int iters, int reps, float *ms_per_gemv) {
-    if (!ws || nw <= 0 || !x || !y || n < 1 || n > 2 || iters <= 0 || reps <= 0 || !ms_per_gemv) {
+    if (!ws || nw <= 0 || !x || !y || n < 1 || n > 16 || iters <= 0 || reps <= 0 || !ms_per_gemv) {
         cmolcu_set_error("cmolcu_gemv_bench: bad arguments");
         return -1;
     }
@@ -308,7 +309,7 @@ extern "C" int cmolcu_gemv_bench(cmolcu_weight_t *const *ws, int nw, const float
             a.x = x; a.x_ld = q.k; a.x_inc = 1; a.ncol = n;
             a.y = y; a.y_ld = q.rows; a.y_inc = 1;
             a.fault = fw;
-            cudaError_t e = gemv_launch(a, EPI_STORE, st, true);
+            cudaError_t e = gemv_launch_cols(a, n, EPI_STORE, st, true);   // the engine's column loop
             if (e != cudaSuccess) return e;
         }
         return cudaSuccess;
