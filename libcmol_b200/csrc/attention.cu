@@ -268,8 +268,14 @@ cudaError_t attention_launch(const AttnArgs &a_in, int ncol, cudaStream_t st, bo
     // step has more (column, kv head) pairs to spread over the SMs.
     if (!a.grouped && !force_list && !split_items && (a.d_head == 64 || a.d_head == 128) &&
         DEC_SUB % a.page_tokens == 0 && a.split_tokens <= DEC_SUB) {
+        // CMOLCU_ATTN_SUBS fixes the 64-token sub-tiles a chunk (measurement switch)
+        static const int subs_knob = [] {
+            const char *v = getenv("CMOLCU_ATTN_SUBS");
+            return v && *v ? atoi(v) : 0;
+        }();
         int subs = 1;
         while (subs < 8 && ncol * a.n_kv >= 64 * subs) subs <<= 1;
+        if (subs_knob == 1 || subs_knob == 2 || subs_knob == 4 || subs_knob == 8) subs = subs_knob;
         a.chunk_tokens = DEC_SUB * subs;
         const bool h = a.kv_f16 != 0;
         if (h && a.tc_min_cols > 0 && ncol >= a.tc_min_cols && a.order && a.work &&
