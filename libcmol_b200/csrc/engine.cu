@@ -658,13 +658,23 @@ static void attention_plan(int *m, const std::vector<StepColumn> &cols, int B, i
     for (int i = 0; i < (int)cols.size(); i++)
         if (cols[i].pos >= 0) order[nl++] = i;
     std::stable_sort(order, order + nl, [&](int x, int y) { return cols[x].pos > cols[y].pos; });
-    const long long target = 6LL * device_sm_count();
+    // CMOLCU_ATTN_ITEMS_PER_SM / CMOLCU_ATTN_CHUNK_MAX: measurement switches
+    static const int per_sm = [] {
+        const char *v = getenv("CMOLCU_ATTN_ITEMS_PER_SM");
+        return v && atoi(v) > 0 ? atoi(v) : 6;
+    }();
+    static const int ch_max = [] {
+        const char *v = getenv("CMOLCU_ATTN_CHUNK_MAX");
+        const int c = v ? atoi(v) : 0;
+        return c >= 64 && c <= 4096 && (c & (c - 1)) == 0 ? c : 4096;
+    }();
+    const long long target = (long long)per_sm * device_sm_count();
     auto items = [&](int c) {
         long long t = 0;
         for (int r = 0; r < nl; r++) t += cols[order[r]].pos / c + 1;
         return t * n_kv;
     };
-    int ch = 4096;                                // at most 256 pages an item (its page list in shared memory)
+    int ch = ch_max;                              // at most 256 pages an item (its page list in shared memory)
     while (ch > 256 * page_tokens) ch >>= 1;
     while (ch > 64 && items(ch) < target) ch >>= 1;
     pfx[0] = 0;
